@@ -1,0 +1,254 @@
+/*
+ * tir.h -- C ABI of the B200 (sm_100a) decode runtime for the Q8_0 Llama-2
+ * path of ZeroR0R/tensor-inference-runtime.
+ *
+ * The reference is an in-process Rust crate; every entry point below names the
+ * reference function (path:line within that crate) it replaces.  Plain
+ * pointers and sizes only.  Unless stated otherwise:
+ *   - "host" pointers are ordinary CPU memory, "device" pointers are CUDA
+ *     global memory on the device the object was created on;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default);
+ *   - functions return tir_status; on failure tir_last_error() returns a
+ *     thread-local message formatted like the reference's thiserror Display.
+ * The library owns all memory it allocates.  A tir_state is not thread-safe;
+ * distinct states may be driven from distinct host threads.
+ */
+#ifndef TIR_H
+#define TIR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (src/error.rs) ----------------------------------------- */
+typedef enum tir_status {
+    TIR_OK = 0,
+    /* ReaderError, src/error.rs:5-24 */
+    TIR_ERR_UNEXPECTED_EOF = 1,
+    TIR_ERR_INVALID_UTF8 = 2,
+    TIR_ERR_BAD_MAGIC = 3,
+    TIR_ERR_BAD_VERSION = 4,
+    TIR_ERR_UNSUPPORTED_TYPE = 5,
+    TIR_ERR_UNSUPPORTED_DTYPE = 6,
+    TIR_ERR_BAD_QUANT_BLOCK = 7,
+    /* MetaDataError, src/error.rs:27-36 */
+    TIR_ERR_MISSING_FIELD = 8,
+    TIR_ERR_WRONG_TYPE = 9,
+    /* ModelLoadError::TensorDataError, src/error.rs:52-53 */
+    TIR_ERR_TENSOR_DATA = 10,
+    /* ForwardPassError::TensorLoadError, src/error.rs:60-61 */
+    TIR_ERR_TENSOR_LOAD = 11,
+    /* TokenizerError::UnknownId (src/error.rs:44-45); also an out-of-range id
+     * that the reference's embed() would panic on (src/tokenizer.rs:15) */
+    TIR_ERR_BAD_TOKEN = 12,
+    /* std::io::Error from read_gguf (src/reader.rs:15-21) */
+    TIR_ERR_IO = 13,
+    /* runtime conditions with no reference counterpart */
+    TIR_ERR_CUDA = 20,
+    TIR_ERR_OOM = 21,
+    TIR_ERR_CTX_OVERFLOW = 22,  /* pos >= the state's max_ctx */
+    TIR_ERR_INVALID_ARG = 23,
+    TIR_ERR_UNSUPPORTED_SHAPE = 24,
+    TIR_ERR_TIMEOUT = 25,       /* a bounded device-side wait gave up */
+    TIR_ERR_NO_DEVICE = 26
+} tir_status;
+
+/* Thread-local message of the last failing call on this thread. */
+const char *tir_last_error(void);
+/* Version string of this library. */
+const char *tir_version(void);
+
+/* ---- GGUF reader (src/reader.rs, src/lib.rs:29-138, src/state.rs) -------- */
+
+/* GgufMetadataValueType, src/state.rs:28-56 */
+enum {
+    TIR_GGUF_U8 = 0, TIR_GGUF_I8 = 1, TIR_GGUF_U16 = 2, TIR_GGUF_I16 = 3,
+    TIR_GGUF_U32 = 4, TIR_GGUF_I32 = 5, TIR_GGUF_F32 = 6, TIR_GGUF_BOOL = 7,
+    TIR_GGUF_STRING = 8, TIR_GGUF_ARRAY = 9, TIR_GGUF_U64 = 10, TIR_GGUF_I64 = 11,
+    TIR_GGUF_F64 = 12
+};
+/* Tensor dtypes the reference accepts (src/reader.rs:247-253). */
+enum { TIR_DTYPE_F32 = 0, TIR_DTYPE_Q8_0 = 8 };
+
+typedef struct tir_gguf tir_gguf;
+
+/* MetaDataField (src/state.rs:9-14) with the value widened: `u` holds
+ * U8/U16/U32/U64/BOOL, `i` holds I8/I16/I32/I64, `f` holds F32/F64 (F32
+ * exactly), `str`/`str_len` hold STRING (not NUL-terminated), and
+ * `array_type`/`array_len` describe ARRAY (items via tir_gguf_metadata_item). */
+typedef struct tir_metadata_field {
+    const char *name;
+    uint32_t vtype;
+    uint64_t u;
+    int64_t i;
+    double f;
+    const char *str;
+    uint64_t str_len;
+    uint32_t array_type;
+    uint64_t array_len;
+} tir_metadata_field;
+
+/* Tensor (src/data.rs:3-9): `n_dims` is the reference's `n_elements` field. */
+typedef struct tir_tensor_info {
+    const char *name;
+    uint32_t n_dims;
+    uint64_t shape[8];
+    uint32_t dtype;
+    uint64_t offset;      /* relative to the aligned data start */
+    uint64_t data_bytes;  /* parse_tensor_data's slice length */
+} tir_tensor_info;
+
+/* Transformer (src/data.rs:25-33) plus the sizes the reference hard-codes
+ * (src/forward.rs:46,54,250; src/math.rs:165), read from tensor shapes. */
+typedef struct tir_transformer {
+    uint32_t layers;
+    uint64_t dim;        /* head / rope dimension (llama.rope.dimension_count) */
+    uint64_t embed_dim;
+    uint64_t q_heads;
+    uint64_t k_v_heads;
+    float base_freq;
+    int32_t mode;        /* Mode, src/data.rs:16-20: 0 Normal, 1 Quantize */
+    uint64_t kv_dim;     /* k_v_heads * dim */
+    uint64_t ffn_dim;
+    uint64_t vocab;
+} tir_transformer;
+
+/* read_gguf + load_model's parse (src/reader.rs:15, src/lib.rs:29-138):
+ * checks magic/version, parses metadata, the Transformer fields, tensor infos
+ * and every tensor's data bounds.  The file is read into host memory. */
+tir_status tir_gguf_open(const char *path, tir_gguf **out);
+/* Same over a caller buffer; the bytes are copied. */
+tir_status tir_gguf_open_bytes(const uint8_t *data, size_t len, tir_gguf **out);
+void tir_gguf_close(tir_gguf *g);
+/* parse_general (src/reader.rs:98-169) alone, over `count` fields starting at
+ * `offset` of `data`; returns a handle holding only metadata and the offset
+ * just past the last field. */
+tir_status tir_gguf_parse_general(const uint8_t *data, size_t len, size_t offset,
+                                  uint64_t count, tir_gguf **out, size_t *end_offset);
+/* parse_q8 (src/reader.rs:258-272): byte length of `count` Q8_0 weights. */
+tir_status tir_gguf_parse_q8(uint64_t count, size_t byte_count, size_t map_len, size_t offset,
+                             size_t *out_len);
+uint32_t tir_gguf_version(const tir_gguf *g);
+int64_t tir_gguf_n_metadata(const tir_gguf *g);
+tir_status tir_gguf_metadata(const tir_gguf *g, int64_t i, tir_metadata_field *out);
+tir_status tir_gguf_metadata_item(const tir_gguf *g, int64_t i, uint64_t j,
+                                  tir_metadata_field *out);
+int64_t tir_gguf_n_tensors(const tir_gguf *g);
+tir_status tir_gguf_tensor_info(const tir_gguf *g, int64_t i, tir_tensor_info *out);
+/* The HashMap<String,&[u8]> lookup of get_tensor (src/forward.rs:277-285):
+ * TIR_ERR_TENSOR_LOAD if `name` is absent.  Host pointer into the handle. */
+tir_status tir_gguf_tensor_data(const tir_gguf *g, const char *name, const uint8_t **data,
+                                size_t *len);
+/* load_model's Transformer extraction (src/lib.rs:70-115). */
+tir_status tir_gguf_transformer(const tir_gguf *g, tir_transformer *out);
+
+/* ---- model: weights resident in HBM --------------------------------------- */
+typedef struct tir_model tir_model;
+
+/* read_gguf + load_model (src/reader.rs:15, src/lib.rs:29): parse, repack
+ * Q8_0 into the runtime's split layout and upload once to HBM on `device`. */
+tir_status tir_model_load(const char *path, int device, tir_model **out);
+tir_status tir_model_load_gguf(const tir_gguf *g, int device, tir_model **out);
+tir_status tir_model_info(const tir_model *m, tir_transformer *out);
+/* Mode switch (the q_act cargo feature, src/lib.rs:99-103). */
+tir_status tir_model_set_mode(tir_model *m, int32_t mode);
+/* Device bytes held by the model's weights. */
+uint64_t tir_model_weight_bytes(const tir_model *m);
+void tir_model_destroy(tir_model *m);
+
+/* ---- state: the KV cache (src/data.rs:41-51 Cache) ----------------------- */
+typedef struct tir_state tir_state;
+
+/* Cache::new (src/data.rs:48), bounded: one sequence, positions < max_ctx. */
+tir_status tir_state_create(tir_model *m, int32_t max_ctx, tir_state **out);
+/* Empties the cache (next forward is pos 0). */
+tir_status tir_state_reset(tir_state *s);
+/* Number of cached positions. */
+int32_t tir_state_len(const tir_state *s);
+/* The CUDA stream (cudaStream_t) every call on this state is ordered on. */
+void *tir_state_stream(tir_state *s);
+void tir_state_destroy(tir_state *s);
+
+/* forward (src/forward.rs:13-258) with the input already embedded:
+ * x_host = embed_dim floats, pos must equal tir_state_len(s).
+ * logits_host (optional) receives vocab floats. */
+tir_status tir_forward_embedded(tir_state *s, const float *x_host, int32_t pos,
+                                float *logits_host);
+/* embed (src/tokenizer.rs:10) + forward: token id in, logits out. */
+tir_status tir_forward(tir_state *s, int32_t token_id, int32_t pos, float *logits_host);
+/* generate_capped (src/lib.rs:239-314) on token ids: token-by-token prompt
+ * pass then greedy decode of `cap` ids into out_ids_host.  The whole loop runs
+ * on the device in one launch; only ids cross the boundary.  Starts from an
+ * empty cache.  last_logits_host (optional): logits of the final forward. */
+tir_status tir_generate_capped(tir_state *s, const int32_t *prompt_host, int32_t n_prompt,
+                               int32_t cap, int32_t *out_ids_host, float *last_logits_host);
+/* Same with device buffers, asynchronous on tir_state_stream(s). */
+tir_status tir_generate_capped_device(tir_state *s, const int32_t *prompt_dev, int32_t n_prompt,
+                                      int32_t cap, int32_t *out_ids_dev);
+/* Waits for the state's stream and reports a device-side timeout, if any
+ * (use after tir_generate_capped_device). */
+tir_status tir_state_sync(tir_state *s);
+/* test_forward (src/lib.rs:316-328): all-ones embedding at pos 0 on an empty
+ * cache, argmax of the logits. */
+tir_status tir_test_forward(tir_state *s, int32_t *out_id);
+/* Residual stream of the last forward: (layers+1) x embed_dim floats, the
+ * input and the output of every layer (the per-layer dump of
+ * save_intermediate, src/forward.rs:287-308).  Enable before the forward. */
+tir_status tir_state_enable_dump(tir_state *s, int32_t enable);
+tir_status tir_state_dump(tir_state *s, float *out_host);
+
+/* ---- op-level kernels (device pointers, asynchronous on `stream`) --------- */
+
+/* Q8_0 blocks (34 B: f16 scale LE + 32 int8) of a [rows][k] tensor into the
+ * runtime's split layout: quants [rows][k] uint8 holding q+128, scales
+ * [rows][scale_stride] f16 with scale_stride = tir_q8_scale_stride(k). */
+int64_t tir_q8_scale_stride(int64_t k);
+tir_status tir_q8_repack(const uint8_t *blocks, int64_t rows, int64_t k, uint8_t *quants,
+                         uint16_t *scales, void *stream);
+/* q8_matmul (src/math.rs:87-98): out[n] = sum_b f32(s[n,b]) * sum_i x[32b+i]*q[n,b,i].
+ * Streaming sm_100a GEMV over the split layout. */
+tir_status tir_q8_matmul(const float *x, const uint8_t *quants, const uint16_t *scales,
+                         float *out, int64_t n, int64_t k, void *stream);
+/* q8_full_dequant / q8_dequant_block (src/math.rs:117-137): bit-exact. */
+tir_status tir_q8_dequant(const uint8_t *blocks, int64_t n_blocks, float *out, void *stream);
+/* embed (src/tokenizer.rs:10-32): row `id` of a Q8_0 [vocab][dim] table. */
+tir_status tir_embed(const uint8_t *blocks, int64_t vocab, int64_t id, int64_t dim, float *out,
+                     void *stream);
+/* rmsnorm (src/math.rs:141-150). */
+tir_status tir_rmsnorm(const float *x, const float *w, float *out, int64_t n, void *stream);
+/* softmax (src/math.rs:153-161). */
+tir_status tir_softmax(const float *x, float *out, int64_t n, void *stream);
+/* rope (src/math.rs:196-228) in place; thetas = dim/2 angles (rope_angles). */
+tir_status tir_rope(float *q, int64_t nq, float *k, int64_t nk, const float *thetas, int64_t dim,
+                    void *stream);
+/* rope_angles (src/math.rs:181-193), host: dim/2 floats into out_host. */
+void tir_rope_angles(float base, int64_t pos, int64_t dim, float *out_host);
+/* swiglu (src/math.rs:164-178) over split-layout gate/up ([f][k]) and down
+ * ([k][f]) matrices. */
+tir_status tir_swiglu(const float *x, const uint8_t *gate_q, const uint16_t *gate_s,
+                      const uint8_t *up_q, const uint16_t *up_s, const uint8_t *down_q,
+                      const uint16_t *down_s, float *out, int64_t k, int64_t f, void *stream);
+/* activated_q8 (src/kernels.rs:8-31): k floats -> k/32 Q8_0 blocks, bit-exact. */
+tir_status tir_activated_q8(const float *x, int64_t k, uint8_t *out_blocks, void *stream);
+/* q8_act_matmul (src/math.rs:101-112): quantised activation (Q8_0 blocks) x
+ * split-layout weights; exact integer block dots, reference block order. */
+tir_status tir_q8_act_matmul(const uint8_t *x_blocks, const uint8_t *quants,
+                             const uint16_t *scales, float *out, int64_t n, int64_t k,
+                             void *stream);
+/* sample (src/tokenizer.rs:152-167): argmax by total order, last of equal
+ * maxima; n == 0 gives 0. */
+tir_status tir_argmax(const float *x, int64_t n, int32_t *out_id, void *stream);
+/* Grouped-query decode attention (src/forward.rs:86-174) for one position:
+ * q [q_heads*dim], caches [k_v_heads][max_ctx][dim] holding n_ctx positions,
+ * out [q_heads*dim]. */
+tir_status tir_attention(const float *q, const float *k_cache, const float *v_cache,
+                         float *out, int64_t q_heads, int64_t k_v_heads, int64_t dim,
+                         int64_t n_ctx, int64_t max_ctx, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,1042 @@
+// api.cpp -- the extern "C" boundary (include/tir.h): GGUF handles, model
+// upload to HBM, the KV-cache state, the forward/generate drivers and the
+// op-level entry points.  No compute happens on the host except what the
+// reference itself does on the host (rope_angles, src/math.rs:181-193, and the
+// cos/sin of those angles, evaluated with the same glibc libm).
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "host.h"
+#include "runtime.h"
+
+#define TIR_VERSION "0.1.0-sm100a"
+
+namespace tir {
+
+static thread_local std::string g_error;
+
+tir_status fail(tir_status st, const std::string& msg) {
+    g_error = msg;
+    return st;
+}
+
+void clear_error() { g_error.clear(); }
+
+static tir_status cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? TIR_ERR_OOM : TIR_ERR_CUDA,
+                std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+#define CUDA_TRY(expr, what)                         \
+    do {                                             \
+        cudaError_t e_ = (expr);                     \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+static int tile_rows_max(int64_t k) {
+    const int64_t per = k + scale_stride(k) * 2;
+    int64_t r = kStageBytes / per;
+    if (r > kMaxTileRows) r = kMaxTileRows;
+    return static_cast<int>(r) & ~1;
+}
+
+int tile_rows_for(int64_t k, int64_t n, int grid) {
+    int r = tile_rows_max(k);
+    if (grid > 0) {
+        int64_t want = (n + grid - 1) / grid;
+        want = (want + 1) & ~int64_t(1);
+        if (want < 2) want = 2;
+        if (want < r) r = static_cast<int>(want);
+    }
+    return r;
+}
+
+// rope_angles (src/math.rs:181-193) and cosf/sinf of each angle, exactly as
+// the reference evaluates them per token (src/math.rs:207-208, glibc libm).
+void rope_table(float base, int64_t dim, int64_t max_ctx, std::vector<float>& c, std::vector<float>& s) {
+    const int64_t half = dim / 2;
+    c.assign(static_cast<size_t>(max_ctx * half), 0.f);
+    s.assign(static_cast<size_t>(max_ctx * half), 0.f);
+    std::vector<float> freq(static_cast<size_t>(half));
+    for (int64_t i = 0; i < half; ++i)
+        freq[i] = powf(base, (-2.0f * static_cast<float>(i)) / static_cast<float>(dim));
+    for (int64_t pos = 0; pos < max_ctx; ++pos)
+        for (int64_t i = 0; i < half; ++i) {
+            const float theta = static_cast<float>(pos) * freq[i];
+            c[pos * half + i] = cosf(theta);
+            s[pos * half + i] = sinf(theta);
+        }
+}
+
+// Small per-device buffers for the single-phase streaming matvec.
+struct DevCtx {
+    uint32_t* counters = nullptr;  // [1]
+    uint32_t* error = nullptr;     // [4]
+    unsigned long long* argmax = nullptr;
+};
+
+static DevCtx* dev_ctx(int device) {
+    static std::mutex mu;
+    static std::vector<DevCtx*> ctxs;
+    std::lock_guard<std::mutex> lock(mu);
+    if (device >= static_cast<int>(ctxs.size())) ctxs.resize(device + 1, nullptr);
+    if (!ctxs[device]) {
+        DevCtx* c = new DevCtx;
+        if (cudaMalloc(&c->counters, 64) != cudaSuccess || cudaMalloc(&c->error, 64) != cudaSuccess ||
+            cudaMalloc(&c->argmax, 8 * 1024) != cudaSuccess) {
+            delete c;
+            return nullptr;
+        }
+        cudaMemset(c->counters, 0, 64);
+        cudaMemset(c->error, 0, 64);
+        ctxs[device] = c;
+    }
+    return ctxs[device];
+}
+
+static unsigned long long timeout_ns() {
+    const char* e = std::getenv("TIR_TIMEOUT_MS");
+    long long ms = e ? std::atoll(e) : 2000;
+    if (ms <= 0) ms = 2000;
+    return static_cast<unsigned long long>(ms) * 1000000ull;
+}
+
+tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out, int64_t n,
+                            int64_t k, void* stream) {
+    if (n == 0) return TIR_OK;
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    DevCtx* c = dev_ctx(dev);
+    if (!c) return fail(TIR_ERR_OOM, "device context allocation failed");
+    const int sms = decode_grid_size(dev);
+    DecodeParams p{};
+    PhaseDesc& d = p.single;
+    d.kind = PH_GEMV;
+    d.in_kind = IN_RAW;
+    d.epi = EPI_STORE;
+    d.n = static_cast<int32_t>(n);
+    d.k = static_cast<int32_t>(k);
+    d.sk = static_cast<int32_t>(scale_stride(k));
+    d.rows_per_tile = tile_rows_for(k, n, sms);
+    d.n_tiles = static_cast<int32_t>((n + d.rows_per_tile - 1) / d.rows_per_tile);
+    d.segs = static_cast<int32_t>((k + kSegK - 1) / kSegK);
+    d.wq = quants;
+    d.ws = scales;
+    d.in = x;
+    d.out = out;
+    p.phases = nullptr;
+    p.n_phases = 1;
+    p.n_steps = 1;
+    p.counters = c->counters;
+    p.error = c->error;
+    p.argmax_part = c->argmax;
+    p.timeout_ns = timeout_ns();
+    const int grid = d.n_tiles < sms ? d.n_tiles : sms;
+    const int rc = decode_launch(p, grid, stream, false);
+    if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "q8 matvec launch");
+    return TIR_OK;
+}
+
+}  // namespace tir
+
+using namespace tir;
+
+// ---------------------------------------------------------------------------
+// model / state objects
+// ---------------------------------------------------------------------------
+struct Mat {
+    uint8_t* q = nullptr;
+    uint16_t* s = nullptr;
+    int64_t n = 0, k = 0, sk = 0;
+};
+
+struct tir_model {
+    int device = 0;
+    tir_transformer t{};
+    uint8_t* dev = nullptr;
+    size_t dev_bytes = 0;
+    uint64_t weight_bytes = 0;  // quants + scales + norm weights
+    std::vector<Mat> qkv, o, gu, down;
+    Mat lm, embd;
+    std::vector<float*> attn_norm, ffn_norm;
+    float* out_norm = nullptr;
+    ~tir_model() {
+        if (dev) {
+            cudaSetDevice(device);
+            cudaFree(dev);
+        }
+    }
+};
+
+struct tir_state {
+    tir_model* m = nullptr;
+    int32_t max_ctx = 0;
+    int grid = 0;
+    int max_splits = 1;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocs;
+    float *x = nullptr, *x0 = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
+    float *dump = nullptr, *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    float* attn_part = nullptr;
+    uint32_t *attn_cnt = nullptr, *counters = nullptr, *error = nullptr;
+    unsigned long long* argmax_part = nullptr;
+    int32_t *prompt = nullptr, *out_ids = nullptr, *tmp_id = nullptr;
+    PhaseDesc* d_phases = nullptr;
+    int n_phases = 0;
+    int32_t len = 0;
+    bool dump_on = false;
+    int32_t* h_ids = nullptr;  // pinned, max_ctx
+    uint32_t* h_err = nullptr; // pinned, 4
+    ~tir_state() {
+        cudaSetDevice(m ? m->device : 0);
+        if (stream) cudaStreamSynchronize(stream);
+        for (void* p : allocs) cudaFree(p);
+        if (h_ids) cudaFreeHost(h_ids);
+        if (h_err) cudaFreeHost(h_err);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+extern "C" {
+
+const char* tir_last_error(void) { return g_error.c_str(); }
+const char* tir_version(void) { return TIR_VERSION; }
+
+// ---------------------------------------------------------------------------
+// GGUF
+// ---------------------------------------------------------------------------
+tir_status tir_gguf_open(const char* path, tir_gguf** out) {
+    clear_error();
+    if (!path || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return fail(TIR_ERR_IO, std::string("cannot open ") + path + ": " + std::strerror(errno));
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+        close(fd);
+        return fail(TIR_ERR_IO, std::string("cannot stat ") + path);
+    }
+    tir_gguf* g = new tir_gguf;
+    if (st.st_size > 0) {
+        void* base = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_PRIVATE, fd, 0);
+        if (base == MAP_FAILED) {
+            close(fd);
+            delete g;
+            return fail(TIR_ERR_IO, std::string("cannot map ") + path);
+        }
+        g->map_base = base;
+        g->map_len = static_cast<size_t>(st.st_size);
+        g->data = static_cast<const uint8_t*>(base);
+        g->len = g->map_len;
+    }
+    close(fd);
+    const tir_status rc = gguf_parse_all(g);
+    if (rc != TIR_OK) {
+        delete g;
+        return rc;
+    }
+    *out = g;
+    return TIR_OK;
+}
+
+tir_status tir_gguf_open_bytes(const uint8_t* data, size_t len, tir_gguf** out) {
+    clear_error();
+    if ((!data && len) || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    tir_gguf* g = new tir_gguf;
+    g->owned.assign(data, data + len);
+    g->data = g->owned.data();
+    g->len = len;
+    const tir_status rc = gguf_parse_all(g);
+    if (rc != TIR_OK) {
+        delete g;
+        return rc;
+    }
+    *out = g;
+    return TIR_OK;
+}
+
+void tir_gguf_close(tir_gguf* g) { delete g; }
+
+tir_status tir_gguf_parse_general(const uint8_t* data, size_t len, size_t offset, uint64_t count, tir_gguf** out,
+                                  size_t* end_offset) {
+    clear_error();
+    if ((!data && len) || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    tir_gguf* g = new tir_gguf;
+    g->owned.assign(data, data + len);
+    g->data = g->owned.data();
+    g->len = len;
+    size_t end = 0;
+    const tir_status rc = gguf_parse_general(g->data, len, offset, count, g->fields, end);
+    if (rc != TIR_OK) {
+        delete g;
+        return rc;
+    }
+    if (end_offset) *end_offset = end;
+    *out = g;
+    return TIR_OK;
+}
+
+tir_status tir_gguf_parse_q8(uint64_t count, size_t byte_count, size_t map_len, size_t offset, size_t* out_len) {
+    clear_error();
+    // src/reader.rs:258-272
+    if (count % 32 != 0)
+        return fail(TIR_ERR_BAD_QUANT_BLOCK, "q8_0 tensor length " + std::to_string(count) + " is not a multiple of 32");
+    const size_t total = static_cast<size_t>(count / 32) * byte_count;
+    size_t end;
+    if (__builtin_add_overflow(offset, total, &end) || end > map_len)
+        return fail(TIR_ERR_UNEXPECTED_EOF, "unexpected end of file reading q8_0 tensor data at offset " + std::to_string(offset));
+    if (out_len) *out_len = total;
+    return TIR_OK;
+}
+
+uint32_t tir_gguf_version(const tir_gguf* g) { return g ? g->version : 0; }
+int64_t tir_gguf_n_metadata(const tir_gguf* g) { return g ? static_cast<int64_t>(g->fields.size()) : 0; }
+
+static void fill_field(const std::string* name, const MetaValue& v, tir_metadata_field* out) {
+    std::memset(out, 0, sizeof(*out));
+    out->name = name ? name->c_str() : nullptr;
+    out->vtype = v.vtype;
+    out->u = v.u;
+    out->i = v.i;
+    out->f = v.f;
+    out->str = v.str.c_str();
+    out->str_len = v.str.size();
+    out->array_type = v.array_type;
+    out->array_len = v.items.size();
+}
+
+tir_status tir_gguf_metadata(const tir_gguf* g, int64_t i, tir_metadata_field* out) {
+    if (!g || !out || i < 0 || i >= static_cast<int64_t>(g->fields.size()))
+        return fail(TIR_ERR_INVALID_ARG, "metadata index out of range");
+    fill_field(&g->fields[i].name, g->fields[i].value, out);
+    return TIR_OK;
+}
+
+tir_status tir_gguf_metadata_item(const tir_gguf* g, int64_t i, uint64_t j, tir_metadata_field* out) {
+    if (!g || !out || i < 0 || i >= static_cast<int64_t>(g->fields.size()) ||
+        j >= g->fields[i].value.items.size())
+        return fail(TIR_ERR_INVALID_ARG, "metadata item out of range");
+    fill_field(nullptr, g->fields[i].value.items[j], out);
+    return TIR_OK;
+}
+
+int64_t tir_gguf_n_tensors(const tir_gguf* g) { return g ? static_cast<int64_t>(g->tensors.size()) : 0; }
+
+tir_status tir_gguf_tensor_info(const tir_gguf* g, int64_t i, tir_tensor_info* out) {
+    if (!g || !out || i < 0 || i >= static_cast<int64_t>(g->tensors.size()))
+        return fail(TIR_ERR_INVALID_ARG, "tensor index out of range");
+    const TensorInfo& t = g->tensors[i];
+    std::memset(out, 0, sizeof(*out));
+    out->name = t.name.c_str();
+    out->n_dims = t.n_dims;
+    for (size_t d = 0; d < t.shape.size() && d < 8; ++d) out->shape[d] = t.shape[d];
+    out->dtype = t.dtype;
+    out->offset = t.offset;
+    out->data_bytes = t.data_bytes;
+    return TIR_OK;
+}
+
+tir_status tir_gguf_tensor_data(const tir_gguf* g, const char* name, const uint8_t** data, size_t* len) {
+    clear_error();
+    if (!g || !name) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    const TensorInfo* t = gguf_find(g, name);
+    if (!t) return fail(TIR_ERR_TENSOR_LOAD, std::string("unable to load tensor: ") + name);  // src/forward.rs:284
+    if (data) *data = t->data;
+    if (len) *len = t->data_bytes;
+    return TIR_OK;
+}
+
+tir_status tir_gguf_transformer(const tir_gguf* g, tir_transformer* out) {
+    if (!g || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (!g->has_transformer) return fail(TIR_ERR_MISSING_FIELD, "Metadata Load error: missing required field: Layers");
+    *out = g->transformer;
+    return TIR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// model
+// ---------------------------------------------------------------------------
+static tir_status need_tensor(const tir_gguf* g, const std::string& name, uint32_t dtype,
+                              std::vector<uint64_t> shape, const TensorInfo** out) {
+    const TensorInfo* t = gguf_find(g, name);
+    if (!t) return fail(TIR_ERR_TENSOR_LOAD, "unable to load tensor: " + name);
+    if (t->dtype != dtype || t->shape != shape) {
+        std::string s = "tensor " + name + " has dtype " + std::to_string(t->dtype) + " shape [";
+        for (size_t i = 0; i < t->shape.size(); ++i) s += (i ? "," : "") + std::to_string(t->shape[i]);
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, s + "], not the Llama-2 layout this runtime serves");
+    }
+    *out = t;
+    return TIR_OK;
+}
+
+static size_t a256(size_t v) { return (v + 255) / 256 * 256; }
+
+tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
+    clear_error();
+    if (!g || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    if (!g->has_transformer) return fail(TIR_ERR_MISSING_FIELD, "Metadata Load error: missing required field: Layers");
+    tir_transformer t = g->transformer;
+    const uint64_t L = t.layers, H = t.embed_dim, hd = t.dim, nq = t.q_heads, nkv = t.k_v_heads;
+    if (hd != static_cast<uint64_t>(kHeadDim) || nq == 0 || nkv == 0 || nq % nkv != 0 || H != nq * hd ||
+        H % 32 != 0 || H > 8192)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE,
+                    "unsupported shape: head dim " + std::to_string(hd) + ", embedding " + std::to_string(H) +
+                        ", heads " + std::to_string(nq) + "/" + std::to_string(nkv) + " (head dim must be 64)");
+    const uint64_t KVD = nkv * hd;
+    const TensorInfo *te, *to, *ton;
+    tir_status rc;
+    if ((rc = need_tensor(g, "token_embd.weight", TIR_DTYPE_Q8_0, {H, t.vocab}, &te)) != TIR_OK) {
+        // vocab comes from output.weight; report whichever is missing.
+        if (!gguf_find(g, "output.weight")) return fail(TIR_ERR_TENSOR_LOAD, "unable to load tensor: output.weight");
+        return rc;
+    }
+    if ((rc = need_tensor(g, "output.weight", TIR_DTYPE_Q8_0, {H, t.vocab}, &to)) != TIR_OK) return rc;
+    if ((rc = need_tensor(g, "output_norm.weight", TIR_DTYPE_F32, {H}, &ton)) != TIR_OK) return rc;
+    const uint64_t F = t.ffn_dim, V = t.vocab;
+    if (F == 0 || F % 32 != 0 || F > 8192 || V == 0 || V > (1u << 30))
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "unsupported ffn/vocab size");
+    struct LT {
+        const TensorInfo *an, *q, *k, *v, *o, *fn, *gt, *up, *dn;
+    };
+    std::vector<LT> lt(L);
+    for (uint64_t l = 0; l < L; ++l) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        LT& x = lt[l];
+        if ((rc = need_tensor(g, p + "attn_norm.weight", TIR_DTYPE_F32, {H}, &x.an)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "attn_q.weight", TIR_DTYPE_Q8_0, {H, H}, &x.q)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "attn_k.weight", TIR_DTYPE_Q8_0, {H, KVD}, &x.k)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "attn_v.weight", TIR_DTYPE_Q8_0, {H, KVD}, &x.v)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "attn_output.weight", TIR_DTYPE_Q8_0, {H, H}, &x.o)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "ffn_norm.weight", TIR_DTYPE_F32, {H}, &x.fn)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "ffn_gate.weight", TIR_DTYPE_Q8_0, {H, F}, &x.gt)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "ffn_up.weight", TIR_DTYPE_Q8_0, {H, F}, &x.up)) != TIR_OK) return rc;
+        if ((rc = need_tensor(g, p + "ffn_down.weight", TIR_DTYPE_Q8_0, {F, H}, &x.dn)) != TIR_OK) return rc;
+    }
+
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(TIR_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= ndev) return fail(TIR_ERR_INVALID_ARG, "device index out of range");
+    CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+
+    tir_model* m = new tir_model;
+    m->device = device;
+    m->t = t;
+    // Layout: one allocation; each matrix = quants then scales, 256-B aligned.
+    size_t off = 0;
+    auto plan = [&](Mat& mt, int64_t n, int64_t k) {
+        mt.n = n;
+        mt.k = k;
+        mt.sk = scale_stride(k);
+        mt.q = reinterpret_cast<uint8_t*>(off);
+        off = a256(off + static_cast<size_t>(n * k));
+        mt.s = reinterpret_cast<uint16_t*>(off);
+        off = a256(off + static_cast<size_t>(n * mt.sk * 2));
+    };
+    auto plan_f32 = [&](int64_t n) {
+        const size_t at = off;
+        off = a256(off + static_cast<size_t>(n) * 4);
+        return at;
+    };
+    m->qkv.resize(L);
+    m->o.resize(L);
+    m->gu.resize(L);
+    m->down.resize(L);
+    std::vector<size_t> an_off(L), fn_off(L);
+    for (uint64_t l = 0; l < L; ++l) {
+        plan(m->qkv[l], static_cast<int64_t>(H + 2 * KVD), static_cast<int64_t>(H));
+        plan(m->o[l], static_cast<int64_t>(H), static_cast<int64_t>(H));
+        plan(m->gu[l], static_cast<int64_t>(2 * F), static_cast<int64_t>(H));
+        plan(m->down[l], static_cast<int64_t>(H), static_cast<int64_t>(F));
+        an_off[l] = plan_f32(static_cast<int64_t>(H));
+        fn_off[l] = plan_f32(static_cast<int64_t>(H));
+    }
+    plan(m->lm, static_cast<int64_t>(V), static_cast<int64_t>(H));
+    plan(m->embd, static_cast<int64_t>(V), static_cast<int64_t>(H));
+    const size_t on_off = plan_f32(static_cast<int64_t>(H));
+    m->dev_bytes = off;
+    cudaError_t e = cudaMalloc(&m->dev, off);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_fail(e, "weight allocation");
+    }
+    auto fix = [&](Mat& mt) {
+        mt.q = m->dev + reinterpret_cast<size_t>(mt.q);
+        mt.s = reinterpret_cast<uint16_t*>(m->dev + reinterpret_cast<size_t>(mt.s));
+    };
+    for (uint64_t l = 0; l < L; ++l) {
+        fix(m->qkv[l]);
+        fix(m->o[l]);
+        fix(m->gu[l]);
+        fix(m->down[l]);
+        m->attn_norm.push_back(reinterpret_cast<float*>(m->dev + an_off[l]));
+        m->ffn_norm.push_back(reinterpret_cast<float*>(m->dev + fn_off[l]));
+    }
+    fix(m->lm);
+    fix(m->embd);
+    m->out_norm = reinterpret_cast<float*>(m->dev + on_off);
+
+    // Upload: raw Q8_0 bytes to a staging buffer, repacked on the device.
+    size_t staging_bytes = te->data_bytes > to->data_bytes ? te->data_bytes : to->data_bytes;
+    for (const LT& x : lt)
+        for (const TensorInfo* ti : {x.q, x.k, x.v, x.o, x.gt, x.up, x.dn})
+            if (ti->data_bytes > staging_bytes) staging_bytes = ti->data_bytes;
+    uint8_t* staging = nullptr;
+    e = cudaMalloc(&staging, staging_bytes);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_fail(e, "staging allocation");
+    }
+    auto fail_upload = [&](cudaError_t er, const char* what) {
+        cudaFree(staging);
+        delete m;
+        return cuda_fail(er, what);
+    };
+    if ((e = cudaMemset(m->dev, 0, off)) != cudaSuccess) return fail_upload(e, "memset");
+    auto put_mat = [&](const TensorInfo* ti, const Mat& mt, int64_t row0, int64_t step, int64_t roff) -> cudaError_t {
+        const int64_t k = static_cast<int64_t>(ti->shape[0]);
+        const int64_t rows = static_cast<int64_t>(ti->shape[1]);
+        cudaError_t er = cudaMemcpy(staging, ti->data, ti->data_bytes, cudaMemcpyHostToDevice);
+        if (er != cudaSuccess) return er;
+        const int rc2 = launch_repack(staging, rows, k, mt.q + row0 * mt.k, mt.s + row0 * mt.sk, mt.sk, step, roff,
+                                      nullptr);
+        if (rc2 != 0) return static_cast<cudaError_t>(rc2);
+        return cudaDeviceSynchronize();
+    };
+    auto put_f32 = [&](const TensorInfo* ti, float* dst) {
+        return cudaMemcpy(dst, ti->data, ti->data_bytes, cudaMemcpyHostToDevice);
+    };
+    for (uint64_t l = 0; l < L; ++l) {
+        const LT& x = lt[l];
+        if ((e = put_mat(x.q, m->qkv[l], 0, 1, 0)) != cudaSuccess) return fail_upload(e, "upload attn_q");
+        if ((e = put_mat(x.k, m->qkv[l], static_cast<int64_t>(H), 1, 0)) != cudaSuccess) return fail_upload(e, "upload attn_k");
+        if ((e = put_mat(x.v, m->qkv[l], static_cast<int64_t>(H + KVD), 1, 0)) != cudaSuccess) return fail_upload(e, "upload attn_v");
+        if ((e = put_mat(x.o, m->o[l], 0, 1, 0)) != cudaSuccess) return fail_upload(e, "upload attn_output");
+        if ((e = put_mat(x.gt, m->gu[l], 0, 2, 0)) != cudaSuccess) return fail_upload(e, "upload ffn_gate");
+        if ((e = put_mat(x.up, m->gu[l], 0, 2, 1)) != cudaSuccess) return fail_upload(e, "upload ffn_up");
+        if ((e = put_mat(x.dn, m->down[l], 0, 1, 0)) != cudaSuccess) return fail_upload(e, "upload ffn_down");
+        if ((e = put_f32(x.an, m->attn_norm[l])) != cudaSuccess) return fail_upload(e, "upload attn_norm");
+        if ((e = put_f32(x.fn, m->ffn_norm[l])) != cudaSuccess) return fail_upload(e, "upload ffn_norm");
+    }
+    if ((e = put_mat(to, m->lm, 0, 1, 0)) != cudaSuccess) return fail_upload(e, "upload output");
+    if ((e = put_mat(te, m->embd, 0, 1, 0)) != cudaSuccess) return fail_upload(e, "upload token_embd");
+    if ((e = put_f32(ton, m->out_norm)) != cudaSuccess) return fail_upload(e, "upload output_norm");
+    cudaFree(staging);
+    uint64_t wb = 0;
+    auto mb = [](const Mat& mt) { return static_cast<uint64_t>(mt.n * mt.k + mt.n * (mt.k / 32) * 2); };
+    for (uint64_t l = 0; l < L; ++l) wb += mb(m->qkv[l]) + mb(m->o[l]) + mb(m->gu[l]) + mb(m->down[l]) + 8 * H;
+    wb += mb(m->lm) + 4 * H;
+    m->weight_bytes = wb;
+    *out = m;
+    return TIR_OK;
+}
+
+tir_status tir_model_load(const char* path, int device, tir_model** out) {
+    tir_gguf* g = nullptr;
+    tir_status rc = tir_gguf_open(path, &g);
+    if (rc != TIR_OK) return rc;
+    rc = tir_model_load_gguf(g, device, out);
+    tir_gguf_close(g);
+    return rc;
+}
+
+tir_status tir_model_info(const tir_model* m, tir_transformer* out) {
+    if (!m || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    *out = m->t;
+    return TIR_OK;
+}
+
+tir_status tir_model_set_mode(tir_model* m, int32_t mode) {
+    if (!m) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (mode != 0) return fail(TIR_ERR_INVALID_ARG, "Mode::Quantize is not available in the fused decode path yet");
+    m->t.mode = mode;
+    return TIR_OK;
+}
+
+uint64_t tir_model_weight_bytes(const tir_model* m) { return m ? m->weight_bytes : 0; }
+
+void tir_model_destroy(tir_model* m) { delete m; }
+
+// ---------------------------------------------------------------------------
+// state
+// ---------------------------------------------------------------------------
+static tir_status build_phases(tir_state* s) {
+    tir_model* m = s->m;
+    const tir_transformer& t = m->t;
+    const int64_t L = t.layers, H = t.embed_dim, KVD = t.kv_dim;
+    const size_t layer_cache = static_cast<size_t>(t.k_v_heads) * s->max_ctx * kHeadDim;
+    std::vector<PhaseDesc> ph;
+    auto gemv = [&](const Mat& mt, int layer, int32_t in_kind, const float* in, const float* norm_w, int32_t epi,
+                    float* out) {
+        PhaseDesc d{};
+        d.kind = PH_GEMV;
+        d.layer = layer;
+        d.in_kind = in_kind;
+        d.epi = epi;
+        d.n = static_cast<int32_t>(mt.n);
+        d.k = static_cast<int32_t>(mt.k);
+        d.sk = static_cast<int32_t>(mt.sk);
+        d.rows_per_tile = tile_rows_for(mt.k, mt.n, 0);
+        d.n_tiles = static_cast<int32_t>((mt.n + d.rows_per_tile - 1) / d.rows_per_tile);
+        d.segs = static_cast<int32_t>((mt.k + kSegK - 1) / kSegK);
+        d.wq = mt.q;
+        d.ws = mt.s;
+        d.in = in;
+        d.norm_w = norm_w;
+        d.out = out;
+        return d;
+    };
+    for (int64_t l = 0; l < L; ++l) {
+        PhaseDesc q = gemv(m->qkv[l], static_cast<int>(l), l == 0 ? IN_X0_NORM : IN_X_NORM, s->x, m->attn_norm[l],
+                           EPI_QKV, s->q);
+        q.kc = s->kc + l * layer_cache;
+        q.vc = s->vc + l * layer_cache;
+        ph.push_back(q);
+        PhaseDesc a{};
+        a.kind = PH_ATTN;
+        a.layer = static_cast<int>(l);
+        a.kc = q.kc;
+        a.vc = q.vc;
+        ph.push_back(a);
+        ph.push_back(gemv(m->o[l], static_cast<int>(l), IN_RAW, s->attn, nullptr, EPI_RESID, s->x));
+        ph.push_back(gemv(m->gu[l], static_cast<int>(l), IN_X_NORM, s->x, m->ffn_norm[l], EPI_GU, s->h));
+        PhaseDesc dn = gemv(m->down[l], static_cast<int>(l), IN_RAW, s->h, nullptr, EPI_RESID, s->x);
+        dn.dump = 1;
+        ph.push_back(dn);
+    }
+    ph.push_back(gemv(m->lm, -1, L == 0 ? IN_X0_NORM : IN_X_NORM, s->x, m->out_norm, EPI_LOGITS, s->logits));
+    (void)H;
+    (void)KVD;
+    s->n_phases = static_cast<int>(ph.size());
+    void* p = nullptr;
+    CUDA_TRY(cudaMalloc(&p, ph.size() * sizeof(PhaseDesc)), "phase table");
+    s->allocs.push_back(p);
+    s->d_phases = static_cast<PhaseDesc*>(p);
+    CUDA_TRY(cudaMemcpy(p, ph.data(), ph.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice), "phase table upload");
+    void* c = nullptr;
+    CUDA_TRY(cudaMalloc(&c, ph.size() * sizeof(uint32_t)), "phase counters");
+    s->allocs.push_back(c);
+    s->counters = static_cast<uint32_t*>(c);
+    return TIR_OK;
+}
+
+tir_status tir_state_create(tir_model* m, int32_t max_ctx, tir_state** out) {
+    clear_error();
+    if (!m || !out || max_ctx <= 0) return fail(TIR_ERR_INVALID_ARG, "invalid argument");
+    *out = nullptr;
+    CUDA_TRY(cudaSetDevice(m->device), "cudaSetDevice");
+    const tir_transformer& t = m->t;
+    tir_state* s = new tir_state;
+    s->m = m;
+    s->max_ctx = max_ctx;
+    s->grid = decode_grid_size(m->device);
+    int occ = 0;
+    cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete s;
+        return cuda_fail(e, "stream");
+    }
+    const int64_t H = t.embed_dim, V = t.vocab, F = t.ffn_dim, L = t.layers;
+    const int64_t group = t.q_heads / t.k_v_heads;
+    int64_t ms = static_cast<int64_t>(s->grid) / static_cast<int64_t>(t.k_v_heads);
+    const int64_t need = (max_ctx + kAttnChunk - 1) / kAttnChunk;
+    if (ms > need) ms = need;
+    if (ms < 1) ms = 1;
+    s->max_splits = static_cast<int>(ms);
+    auto alloc = [&](size_t bytes, void** p) -> bool {
+        if (cudaMalloc(p, bytes ? bytes : 16) != cudaSuccess) return false;
+        s->allocs.push_back(*p);
+        return true;
+    };
+    const size_t cache_f = static_cast<size_t>(L) * t.k_v_heads * max_ctx * kHeadDim;
+    bool ok = alloc(H * 4, reinterpret_cast<void**>(&s->x)) && alloc(H * 4, reinterpret_cast<void**>(&s->x0)) &&
+              alloc(H * 4, reinterpret_cast<void**>(&s->q)) && alloc(H * 4, reinterpret_cast<void**>(&s->attn)) &&
+              alloc(F * 4, reinterpret_cast<void**>(&s->h)) && alloc(V * 4, reinterpret_cast<void**>(&s->logits)) &&
+              alloc((L + 1) * H * 4, reinterpret_cast<void**>(&s->dump)) &&
+              alloc(cache_f * 4, reinterpret_cast<void**>(&s->kc)) && alloc(cache_f * 4, reinterpret_cast<void**>(&s->vc)) &&
+              alloc(static_cast<size_t>(max_ctx) * 32 * 4, reinterpret_cast<void**>(&s->rope_cos)) &&
+              alloc(static_cast<size_t>(max_ctx) * 32 * 4, reinterpret_cast<void**>(&s->rope_sin)) &&
+              alloc(static_cast<size_t>(t.k_v_heads) * ms * group * (kHeadDim + 2) * 4,
+                    reinterpret_cast<void**>(&s->attn_part)) &&
+              alloc(static_cast<size_t>(L) * t.k_v_heads * 4, reinterpret_cast<void**>(&s->attn_cnt)) &&
+              alloc(16, reinterpret_cast<void**>(&s->error)) &&
+              alloc(static_cast<size_t>(s->grid) * 8, reinterpret_cast<void**>(&s->argmax_part)) &&
+              alloc(static_cast<size_t>(max_ctx) * 4, reinterpret_cast<void**>(&s->prompt)) &&
+              alloc(static_cast<size_t>(max_ctx) * 4, reinterpret_cast<void**>(&s->out_ids)) &&
+              alloc(16, reinterpret_cast<void**>(&s->tmp_id));
+    if (!ok) {
+        delete s;
+        return fail(TIR_ERR_OOM, "state allocation failed (KV cache of " + std::to_string(max_ctx) + " positions)");
+    }
+    if (cudaMallocHost(&s->h_ids, static_cast<size_t>(max_ctx) * 4) != cudaSuccess ||
+        cudaMallocHost(&s->h_err, 16) != cudaSuccess) {
+        delete s;
+        return fail(TIR_ERR_OOM, "pinned host allocation failed");
+    }
+    std::vector<float> c, sn;
+    rope_table(t.base_freq, static_cast<int64_t>(t.dim), max_ctx, c, sn);
+    if (cudaMemcpy(s->rope_cos, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(s->attn_cnt, 0, static_cast<size_t>(L) * t.k_v_heads * 4) != cudaSuccess ||
+        cudaMemset(s->argmax_part, 0, static_cast<size_t>(s->grid) * 8) != cudaSuccess) {
+        delete s;
+        return fail(TIR_ERR_CUDA, "state initialisation failed");
+    }
+    tir_status rc = build_phases(s);
+    if (rc != TIR_OK) {
+        delete s;
+        return rc;
+    }
+    // The persistent kernel needs one CTA per SM resident at once.
+    occ = decode_blocks_per_sm();
+    if (occ < 1) {
+        delete s;
+        return fail(TIR_ERR_CUDA, "the decode kernel cannot be resident on this device (" +
+                                      std::to_string(decode_smem_bytes()) + " B shared memory per CTA)");
+    }
+    *out = s;
+    return TIR_OK;
+}
+
+tir_status tir_state_reset(tir_state* s) {
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    s->len = 0;
+    return TIR_OK;
+}
+
+int32_t tir_state_len(const tir_state* s) { return s ? s->len : 0; }
+void* tir_state_stream(tir_state* s) { return s ? static_cast<void*>(s->stream) : nullptr; }
+void tir_state_destroy(tir_state* s) { delete s; }
+
+static tir_status launch_steps(tir_state* s, int n_steps, int pos0, const float* x0, const int32_t* prompt,
+                               int n_prompt, int32_t* out_ids) {
+    const tir_transformer& t = s->m->t;
+    DecodeParams p{};
+    p.phases = s->d_phases;
+    p.n_phases = s->n_phases;
+    p.n_steps = n_steps;
+    p.pos0 = pos0;
+    p.H = static_cast<int32_t>(t.embed_dim);
+    p.q_heads = static_cast<int32_t>(t.q_heads);
+    p.kv_heads = static_cast<int32_t>(t.k_v_heads);
+    p.group = static_cast<int32_t>(t.q_heads / t.k_v_heads);
+    p.kvd = static_cast<int32_t>(t.kv_dim);
+    p.max_ctx = s->max_ctx;
+    p.vocab = static_cast<int32_t>(t.vocab);
+    p.max_splits = s->max_splits;
+    p.x0 = x0;
+    p.prompt = prompt;
+    p.n_prompt = n_prompt;
+    p.out_ids = out_ids;
+    p.embd_q = s->m->embd.q;
+    p.embd_s = s->m->embd.s;
+    p.embd_sk = static_cast<int32_t>(s->m->embd.sk);
+    p.rms_eps = 1e-5f;  // src/math.rs:144, whatever the file says
+    p.x = s->x;
+    p.dump = s->dump_on ? s->dump : nullptr;
+    p.rope_cos = s->rope_cos;
+    p.rope_sin = s->rope_sin;
+    p.attn_part = s->attn_part;
+    p.attn_cnt = s->attn_cnt;
+    p.attn_out = s->attn;
+    p.q = s->q;
+    p.counters = s->counters;
+    p.argmax_part = s->argmax_part;
+    p.error = s->error;
+    p.timeout_ns = timeout_ns();
+    CUDA_TRY(cudaMemsetAsync(s->counters, 0, static_cast<size_t>(s->n_phases) * 4, s->stream), "counter reset");
+    CUDA_TRY(cudaMemsetAsync(s->error, 0, 16, s->stream), "error reset");
+    CUDA_TRY(cudaMemsetAsync(s->attn_cnt, 0, static_cast<size_t>(t.layers) * t.k_v_heads * 4, s->stream),
+             "attention counter reset");
+    const int rc = decode_launch(p, s->grid, s->stream, true);
+    if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "decode launch");
+    return TIR_OK;
+}
+
+static tir_status finish(tir_state* s) {
+    CUDA_TRY(cudaMemcpyAsync(s->h_err, s->error, 12, cudaMemcpyDeviceToHost, s->stream), "error readback");
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "decode");
+    if (s->h_err[0] == TIR_ERR_BAD_TOKEN) {
+        s->len = 0;
+        return fail(TIR_ERR_BAD_TOKEN, "a token id read on the device (step " +
+                                           std::to_string(static_cast<int>(s->h_err[2])) +
+                                           ") is not in the vocab; the cache was reset");
+    }
+    if (s->h_err[0] != 0) {
+        s->len = 0;
+        return fail(TIR_ERR_TIMEOUT, "device wait timed out (phase " + std::to_string(static_cast<int>(s->h_err[1])) +
+                                         ", step " + std::to_string(static_cast<int>(s->h_err[2])) +
+                                         "); the cache was reset");
+    }
+    return TIR_OK;
+}
+
+tir_status tir_forward_embedded(tir_state* s, const float* x_host, int32_t pos, float* logits_host) {
+    clear_error();
+    if (!s || !x_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (pos != s->len) return fail(TIR_ERR_INVALID_ARG, "pos " + std::to_string(pos) + " does not match the cache length " + std::to_string(s->len));
+    if (pos >= s->max_ctx) return fail(TIR_ERR_CTX_OVERFLOW, "pos " + std::to_string(pos) + " >= max_ctx " + std::to_string(s->max_ctx));
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    const size_t H = s->m->t.embed_dim;
+    CUDA_TRY(cudaMemcpyAsync(s->x0, x_host, H * 4, cudaMemcpyHostToDevice, s->stream), "input upload");
+    tir_status rc = launch_steps(s, 1, pos, s->x0, nullptr, 1, nullptr);
+    if (rc != TIR_OK) return rc;
+    if (logits_host)
+        CUDA_TRY(cudaMemcpyAsync(logits_host, s->logits, s->m->t.vocab * 4, cudaMemcpyDeviceToHost, s->stream),
+                 "logits readback");
+    rc = finish(s);
+    if (rc == TIR_OK) s->len = pos + 1;
+    return rc;
+}
+
+tir_status tir_forward(tir_state* s, int32_t token_id, int32_t pos, float* logits_host) {
+    clear_error();
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (token_id < 0 || static_cast<uint64_t>(token_id) >= s->m->t.vocab)
+        return fail(TIR_ERR_BAD_TOKEN, "token id " + std::to_string(token_id) + " is not in the vocab");
+    if (pos != s->len) return fail(TIR_ERR_INVALID_ARG, "pos " + std::to_string(pos) + " does not match the cache length " + std::to_string(s->len));
+    if (pos >= s->max_ctx) return fail(TIR_ERR_CTX_OVERFLOW, "pos " + std::to_string(pos) + " >= max_ctx " + std::to_string(s->max_ctx));
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    s->h_ids[0] = token_id;
+    CUDA_TRY(cudaMemcpyAsync(s->prompt, s->h_ids, 4, cudaMemcpyHostToDevice, s->stream), "token upload");
+    tir_status rc = launch_steps(s, 1, pos, nullptr, s->prompt, 1, nullptr);
+    if (rc != TIR_OK) return rc;
+    if (logits_host)
+        CUDA_TRY(cudaMemcpyAsync(logits_host, s->logits, s->m->t.vocab * 4, cudaMemcpyDeviceToHost, s->stream),
+                 "logits readback");
+    rc = finish(s);
+    if (rc == TIR_OK) s->len = pos + 1;
+    return rc;
+}
+
+static tir_status check_generate(tir_state* s, int32_t n_prompt, int32_t cap) {
+    if (n_prompt < 0 || cap < 0) return fail(TIR_ERR_INVALID_ARG, "negative length");
+    if (static_cast<int64_t>(n_prompt) + cap > s->max_ctx)
+        return fail(TIR_ERR_CTX_OVERFLOW, "prompt + cap = " + std::to_string(static_cast<int64_t>(n_prompt) + cap) +
+                                              " positions > max_ctx " + std::to_string(s->max_ctx));
+    return TIR_OK;
+}
+
+tir_status tir_generate_capped_device(tir_state* s, const int32_t* prompt_dev, int32_t n_prompt, int32_t cap,
+                                      int32_t* out_ids_dev) {
+    clear_error();
+    if (!s || (n_prompt > 0 && !prompt_dev) || (cap > 0 && !out_ids_dev)) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    tir_status rc = check_generate(s, n_prompt, cap);
+    if (rc != TIR_OK) return rc;
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    s->len = 0;
+    const int n_steps = n_prompt + cap;
+    if (n_steps == 0) return TIR_OK;
+    rc = launch_steps(s, n_steps, 0, nullptr, prompt_dev, n_prompt, out_ids_dev);
+    if (rc == TIR_OK) s->len = n_steps;
+    return rc;
+}
+
+tir_status tir_generate_capped(tir_state* s, const int32_t* prompt_host, int32_t n_prompt, int32_t cap,
+                               int32_t* out_ids_host, float* last_logits_host) {
+    clear_error();
+    if (!s || (n_prompt > 0 && !prompt_host) || (cap > 0 && !out_ids_host)) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    tir_status rc = check_generate(s, n_prompt, cap);
+    if (rc != TIR_OK) return rc;
+    for (int32_t i = 0; i < n_prompt; ++i)
+        if (prompt_host[i] < 0 || static_cast<uint64_t>(prompt_host[i]) >= s->m->t.vocab)
+            return fail(TIR_ERR_BAD_TOKEN, "token id " + std::to_string(prompt_host[i]) + " is not in the vocab");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    s->len = 0;
+    const int n_steps = n_prompt + cap;
+    if (n_steps == 0) return TIR_OK;
+    std::memcpy(s->h_ids, prompt_host, static_cast<size_t>(n_prompt) * 4);
+    if (n_prompt > 0)
+        CUDA_TRY(cudaMemcpyAsync(s->prompt, s->h_ids, static_cast<size_t>(n_prompt) * 4, cudaMemcpyHostToDevice, s->stream),
+                 "prompt upload");
+    rc = launch_steps(s, n_steps, 0, nullptr, s->prompt, n_prompt, s->out_ids);
+    if (rc != TIR_OK) return rc;
+    if (cap > 0)
+        CUDA_TRY(cudaMemcpyAsync(s->h_ids, s->out_ids, static_cast<size_t>(cap) * 4, cudaMemcpyDeviceToHost, s->stream),
+                 "ids readback");
+    if (last_logits_host)
+        CUDA_TRY(cudaMemcpyAsync(last_logits_host, s->logits, s->m->t.vocab * 4, cudaMemcpyDeviceToHost, s->stream),
+                 "logits readback");
+    rc = finish(s);
+    if (rc != TIR_OK) return rc;
+    if (cap > 0) std::memcpy(out_ids_host, s->h_ids, static_cast<size_t>(cap) * 4);
+    s->len = n_steps;
+    return TIR_OK;
+}
+
+tir_status tir_state_sync(tir_state* s) {
+    clear_error();
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    return finish(s);
+}
+
+tir_status tir_test_forward(tir_state* s, int32_t* out_id) {
+    clear_error();
+    if (!s || !out_id) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    s->len = 0;
+    const int64_t H = s->m->t.embed_dim;
+    if (launch_fill_f32(s->x0, 1.0f, H, s->stream) != 0) return fail(TIR_ERR_CUDA, "fill launch");
+    tir_status rc = launch_steps(s, 1, 0, s->x0, nullptr, 1, nullptr);
+    if (rc != TIR_OK) return rc;
+    if (launch_argmax(s->logits, static_cast<int64_t>(s->m->t.vocab), s->tmp_id, s->stream) != 0)
+        return fail(TIR_ERR_CUDA, "argmax launch");
+    CUDA_TRY(cudaMemcpyAsync(s->h_ids, s->tmp_id, 4, cudaMemcpyDeviceToHost, s->stream), "id readback");
+    rc = finish(s);
+    if (rc != TIR_OK) return rc;
+    *out_id = s->h_ids[0];
+    s->len = 1;
+    return TIR_OK;
+}
+
+tir_status tir_state_enable_dump(tir_state* s, int32_t enable) {
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    s->dump_on = enable != 0;
+    return TIR_OK;
+}
+
+tir_status tir_state_dump(tir_state* s, float* out_host) {
+    clear_error();
+    if (!s || !out_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (!s->dump_on) return fail(TIR_ERR_INVALID_ARG, "dump not enabled");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    const size_t n = static_cast<size_t>(s->m->t.layers + 1) * s->m->t.embed_dim;
+    CUDA_TRY(cudaMemcpyAsync(out_host, s->dump, n * 4, cudaMemcpyDeviceToHost, s->stream), "dump readback");
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "dump readback");
+    return TIR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// op-level entry points
+// ---------------------------------------------------------------------------
+static tir_status op_rc(int rc, const char* what) {
+    if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), what);
+    return TIR_OK;
+}
+
+int64_t tir_q8_scale_stride(int64_t k) { return scale_stride(k); }
+
+tir_status tir_q8_repack(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* quants, uint16_t* scales,
+                         void* stream) {
+    clear_error();
+    if (rows < 0 || k < 0 || k % 32 != 0) return fail(TIR_ERR_BAD_QUANT_BLOCK, "q8_0 tensor length " + std::to_string(k) + " is not a multiple of 32");
+    const int64_t sk = scale_stride(k);
+    if (rows > 0 && cudaMemsetAsync(scales, 0, static_cast<size_t>(rows * sk * 2), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return fail(TIR_ERR_CUDA, "scale memset");
+    return op_rc(launch_repack(blocks, rows, k, quants, scales, sk, 1, 0, stream), "repack");
+}
+
+tir_status tir_q8_matmul(const float* x, const uint8_t* quants, const uint16_t* scales, float* out, int64_t n,
+                         int64_t k, void* stream) {
+    clear_error();
+    if (n < 0 || k <= 0 || k % 32 != 0 || k > kMaxSegs * kSegK)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "q8 matvec needs 0 < k <= 8192, k % 32 == 0");
+    if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
+    return q8_matmul_stream(x, quants, scales, out, n, k, stream);
+}
+
+tir_status tir_q8_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, void* stream) {
+    clear_error();
+    if (n_blocks < 0) return fail(TIR_ERR_INVALID_ARG, "negative size");
+    return op_rc(launch_dequant(blocks, n_blocks, out, stream), "dequant");
+}
+
+tir_status tir_embed(const uint8_t* blocks, int64_t vocab, int64_t id, int64_t dim, float* out, void* stream) {
+    clear_error();
+    if (dim % 32 != 0) return fail(TIR_ERR_BAD_QUANT_BLOCK, "q8_0 tensor length " + std::to_string(dim) + " is not a multiple of 32");
+    if (id < 0 || id >= vocab) return fail(TIR_ERR_BAD_TOKEN, "token id " + std::to_string(id) + " is not in the vocab");
+    const int64_t row_blocks = dim / 32;
+    return op_rc(launch_dequant(blocks + id * row_blocks * 34, row_blocks, out, stream), "embed");
+}
+
+tir_status tir_rmsnorm(const float* x, const float* w, float* out, int64_t n, void* stream) {
+    clear_error();
+    if (n <= 0) return fail(TIR_ERR_INVALID_ARG, "empty input");
+    return op_rc(launch_rmsnorm(x, w, out, n, 1e-5f, stream), "rmsnorm");
+}
+
+tir_status tir_softmax(const float* x, float* out, int64_t n, void* stream) {
+    clear_error();
+    if (n <= 0) return fail(TIR_ERR_INVALID_ARG, "empty input (the reference unwraps on it)");
+    return op_rc(launch_softmax(x, out, n, stream), "softmax");
+}
+
+void tir_rope_angles(float base, int64_t pos, int64_t dim, float* out_host) {
+    for (int64_t i = 0; i < dim / 2; ++i) {
+        const float frequency = powf(base, (-2.0f * static_cast<float>(i)) / static_cast<float>(dim));
+        out_host[i] = static_cast<float>(pos) * frequency;
+    }
+}
+
+tir_status tir_rope(float* q, int64_t nq, float* k, int64_t nk, const float* thetas_host, int64_t dim,
+                    void* stream) {
+    clear_error();
+    if (dim <= 0 || dim % 2 != 0 || dim > 128 || !thetas_host) return fail(TIR_ERR_INVALID_ARG, "rope dim must be even and <= 128");
+    std::vector<float> cs(static_cast<size_t>(dim));
+    for (int64_t i = 0; i < dim / 2; ++i) {
+        cs[i] = cosf(thetas_host[i]);
+        cs[dim / 2 + i] = sinf(thetas_host[i]);
+    }
+    return op_rc(launch_rope(q, nq, k, nk, cs.data(), dim, stream), "rope");
+}
+
+tir_status tir_swiglu(const float* x, const uint8_t* gate_q, const uint16_t* gate_s, const uint8_t* up_q,
+                      const uint16_t* up_s, const uint8_t* down_q, const uint16_t* down_s, float* out, int64_t k,
+                      int64_t f, void* stream) {
+    clear_error();
+    if (k <= 0 || f <= 0 || k % 32 || f % 32 || k > 8192 || f > 8192)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "swiglu needs k, f multiples of 32 and <= 8192");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* tmp = nullptr;
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&tmp), static_cast<size_t>(3 * f) * 4, st), "swiglu scratch");
+    tir_status rc = q8_matmul_stream(x, gate_q, gate_s, tmp, f, k, stream);
+    if (rc == TIR_OK) rc = q8_matmul_stream(x, up_q, up_s, tmp + f, f, k, stream);
+    if (rc == TIR_OK) rc = op_rc(launch_silu_mul(tmp, tmp + f, tmp + 2 * f, f, stream), "silu");
+    if (rc == TIR_OK) rc = q8_matmul_stream(tmp + 2 * f, down_q, down_s, out, k, f, stream);
+    cudaFreeAsync(tmp, st);
+    return rc;
+}
+
+tir_status tir_activated_q8(const float* x, int64_t k, uint8_t* out_blocks, void* stream) {
+    clear_error();
+    if (k < 0 || k % 32 != 0) return fail(TIR_ERR_BAD_QUANT_BLOCK, "q8_0 tensor length " + std::to_string(k) + " is not a multiple of 32");
+    return op_rc(launch_activated_q8(x, k, out_blocks, stream), "activated_q8");
+}
+
+tir_status tir_q8_act_matmul(const uint8_t* x_blocks, const uint8_t* quants, const uint16_t* scales, float* out,
+                             int64_t n, int64_t k, void* stream) {
+    clear_error();
+    if (k <= 0 || k % 32 != 0 || k > 65536) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "k must be a positive multiple of 32");
+    if (n == 0) return TIR_OK;
+    return op_rc(launch_q8_act_matmul(x_blocks, quants, scales, out, n, k, stream), "q8_act_matmul");
+}
+
+tir_status tir_argmax(const float* x, int64_t n, int32_t* out_id, void* stream) {
+    clear_error();
+    if (n < 0) return fail(TIR_ERR_INVALID_ARG, "negative size");
+    return op_rc(launch_argmax(x, n, out_id, stream), "argmax");
+}
+
+tir_status tir_attention(const float* q, const float* k_cache, const float* v_cache, float* out, int64_t q_heads,
+                         int64_t k_v_heads, int64_t dim, int64_t n_ctx, int64_t max_ctx, void* stream) {
+    clear_error();
+    if (dim != kHeadDim) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "attention head dim must be 64");
+    if (q_heads <= 0 || k_v_heads <= 0 || q_heads % k_v_heads != 0 || n_ctx <= 0 || n_ctx > max_ctx)
+        return fail(TIR_ERR_INVALID_ARG, "bad attention shape");
+    return op_rc(launch_attention(q, k_cache, v_cache, out, q_heads, k_v_heads, n_ctx, max_ctx, stream), "attention");
+}
+
+}  // extern "C"

@@ -1,0 +1,98 @@
+// host.h -- host-side internals shared by the C ABI implementation files.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/tir.h"
+
+namespace tir {
+
+// Thread-local error reporting (tir_last_error).
+tir_status fail(tir_status st, const std::string& msg);
+void clear_error();
+
+// ---- GGUF (src/state.rs, src/reader.rs) ------------------------------------
+struct MetaValue {
+    uint32_t vtype = 0;
+    uint64_t u = 0;
+    int64_t i = 0;
+    double f = 0.0;
+    std::string str;
+    uint32_t array_type = 0;
+    std::vector<MetaValue> items;
+};
+
+struct MetaField {
+    std::string name;
+    MetaValue value;
+};
+
+struct TensorInfo {
+    std::string name;
+    uint32_t n_dims = 0;
+    std::vector<uint64_t> shape;
+    uint32_t dtype = 0;
+    uint64_t offset = 0;
+    const uint8_t* data = nullptr;
+    size_t data_bytes = 0;
+};
+
+}  // namespace tir
+
+struct tir_gguf {
+    std::vector<uint8_t> owned;
+    void* map_base = nullptr;
+    size_t map_len = 0;
+    const uint8_t* data = nullptr;
+    size_t len = 0;
+    uint32_t version = 0;
+    std::vector<tir::MetaField> fields;
+    std::vector<tir::TensorInfo> tensors;
+    std::unordered_map<std::string, size_t> index;
+    bool has_transformer = false;
+    tir_transformer transformer{};
+    ~tir_gguf();
+};
+
+namespace tir {
+// Parses a complete file image held by `g` (g->data/len set): load_model's
+// parse (src/lib.rs:29-138).
+tir_status gguf_parse_all(tir_gguf* g);
+// parse_general (src/reader.rs:98-169).
+tir_status gguf_parse_general(const uint8_t* map, size_t len, size_t offset, uint64_t count,
+                              std::vector<MetaField>& out, size_t& end);
+const TensorInfo* gguf_find(const tir_gguf* g, const std::string& name);
+
+// ---- op-level kernel launchers (ops.cu) -------------------------------------
+int launch_repack(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* quants, uint16_t* scales,
+                  int64_t sk, int64_t dst_row_step, int64_t dst_row_off, void* stream);
+int launch_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, void* stream);
+int launch_rmsnorm(const float* x, const float* w, float* out, int64_t n, float eps, void* stream);
+int launch_softmax(const float* x, float* out, int64_t n, void* stream);
+int launch_rope(float* q, int64_t nq, float* k, int64_t nk, const float* cs, int64_t dim,
+                void* stream);
+int launch_activated_q8(const float* x, int64_t k, uint8_t* out, void* stream);
+int launch_q8_act_matmul(const uint8_t* xb, const uint8_t* quants, const uint16_t* scales,
+                         float* out, int64_t n, int64_t k, void* stream);
+int launch_argmax(const float* x, int64_t n, int32_t* out, void* stream);
+int launch_attention(const float* q, const float* kc, const float* vc, float* out, int64_t qh,
+                     int64_t kvh, int64_t n_ctx, int64_t max_ctx, void* stream);
+int launch_silu_mul(const float* gate, const float* up, float* out, int64_t n, void* stream);
+int launch_fill_f32(float* out, float v, int64_t n, void* stream);
+
+// Streaming Q8_0 matvec (decode.cu machinery, one phase).
+tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out,
+                            int64_t n, int64_t k, void* stream);
+
+// Tile rows of a [n][k] split-layout matrix in one ring stage.
+int tile_rows_for(int64_t k, int64_t n, int grid);
+
+// glibc-evaluated RoPE table for positions [0, max_ctx): cos/sin of
+// rope_angles (src/math.rs:181-193).
+void rope_table(float base, int64_t dim, int64_t max_ctx, std::vector<float>& cos_out,
+                std::vector<float>& sin_out);
+
+}  // namespace tir

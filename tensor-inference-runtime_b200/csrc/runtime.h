@@ -1,0 +1,95 @@
+// runtime.h -- device-side program description shared by the host driver
+// (api.cpp) and the persistent sm_100a kernels (decode.cu).
+//
+// A "program" is the ordered list of phases of one forward step.  For the
+// batch-1 decode loop of src/forward.rs:13-258 it is, per layer,
+//   QKV  (rmsnorm -> fused q|k|v Q8_0 matvec -> RoPE -> KV-cache append)
+//   ATTN (grouped-query attention over the cache, split over positions)
+//   O    (output projection + residual)
+//   GU   (rmsnorm -> fused gate|up matvec -> silu(gate)*up)
+//   DOWN (down projection + residual)
+// and finally LM (rmsnorm -> vocabulary matvec -> logits, argmax partials).
+// Each phase of each step is a grid-wide dependency: its CTAs start once every
+// CTA finished the previous phase (monotonic per-phase counters).  Weights never
+// depend on activations, so a producer warp streams every CTA's weight tiles
+// into a shared-memory ring with TMA bulk copies, across phase and step
+// boundaries, while the consumer warps wait on dependencies.
+#pragma once
+#include <cstdint>
+
+namespace tir {
+
+// ---- launch geometry --------------------------------------------------------
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
+constexpr int kStageBytes = 18432;               // one weight tile
+constexpr int kStages = 11;                      // ring depth
+constexpr int kMaxTileRows = 16;
+constexpr int kSegK = 512;                       // k-columns per warp segment
+constexpr int kMaxSegs = 16;                     // k <= 8192
+constexpr int kMaxSegsPerWarp = 2;
+constexpr int kHeadDim = 64;                     // attention head size supported
+constexpr int kAttnChunk = 32;                   // positions per attention chunk
+constexpr int kAttnHeadsPerPass = kConsumerWarps;
+
+enum PhaseKind : int32_t { PH_GEMV = 0, PH_ATTN = 1 };
+enum InKind : int32_t { IN_RAW = 0, IN_X_NORM = 1, IN_X0_NORM = 2 };
+enum EpiKind : int32_t { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GU = 3, EPI_LOGITS = 4 };
+
+// Scale row stride (f16 elements) of the split Q8_0 layout: 16-byte rows.
+__host__ __device__ constexpr int64_t scale_stride(int64_t k) { return ((k / 32) + 7) / 8 * 8; }
+
+struct PhaseDesc {
+    int32_t kind, layer, in_kind, epi;
+    int32_t n, k, sk;          // rows, columns, scale stride (halves)
+    int32_t rows_per_tile, n_tiles, segs;
+    int32_t dump;              // EPI_RESID: also write the residual to the dump
+    int32_t pad_;
+    const uint8_t* wq;         // quants [n][k], q + 128
+    const uint16_t* ws;        // f16 scales [n][sk]
+    const float* in;           // IN_RAW input / IN_X_NORM residual buffer
+    const float* norm_w;       // rmsnorm weights (IN_*_NORM)
+    float* out;                // epilogue target
+    float* kc;                 // EPI_QKV: key cache of this layer [kv][max_ctx][64]
+    float* vc;                 // EPI_QKV: value cache of this layer
+};
+
+struct DecodeParams {
+    const PhaseDesc* phases;   // device array; NULL -> use `single`
+    PhaseDesc single;
+    int32_t n_phases;
+    int32_t n_steps, pos0;
+    int32_t H, q_heads, kv_heads, group, kvd, max_ctx, vocab, max_splits;
+    // token source of each step (IN_X0_NORM): x0 (step 0 only, optional),
+    // else prompt[f] for f < n_prompt, else argmax of the previous logits.
+    const float* x0;
+    const int32_t* prompt;
+    int32_t n_prompt;
+    int32_t* out_ids;          // sampled ids of steps >= n_prompt
+    const uint8_t* embd_q;     // token_embd, split layout
+    const uint16_t* embd_s;
+    int32_t embd_sk;
+    float rms_eps;
+    // state buffers
+    float* x;                  // residual stream [H]
+    float* dump;               // optional [(layers+1)][H]
+    const float* rope_cos;     // [max_ctx][32]
+    const float* rope_sin;
+    float* attn_part;          // [kv][max_splits][group][2 + 64]
+    uint32_t* attn_cnt;        // [layers][kv]
+    float* attn_out;           // [H]
+    const float* q;            // [H] (written by EPI_QKV)
+    uint32_t* counters;        // [n_phases]
+    unsigned long long* argmax_part;  // [grid]
+    uint32_t* error;           // [0] code, [1] phase, [2] step
+    unsigned long long timeout_ns;
+};
+
+// Host launchers (decode.cu).
+int decode_launch(const DecodeParams& p, int grid, void* stream, bool cooperative);
+int decode_grid_size(int device);
+int decode_smem_bytes();
+int decode_blocks_per_sm();
+
+}  // namespace tir
