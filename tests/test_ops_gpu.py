@@ -11,7 +11,7 @@ pytestmark = pytest.mark.gpu
 
 
 def dev(torch, a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return torch.from_numpy(np.array(a, copy=True)).cuda()
 
 
 def host(t):
@@ -118,7 +118,12 @@ def test_rmsnorm(cuda, tirlib, orc, kat, n):
     out = torch.empty(n, dtype=torch.float32, device="cuda")
     tirlib.rmsnorm(dev(torch, x), dev(torch, w), out, n)
     got = host(out)
-    np.testing.assert_allclose(got, orc.rmsnorm(x, w), rtol=2e-6, atol=0)
+    # The oracle's Sigma x^2 is a sequential f32 fold (relative drift ~ sqrt(n) ulp);
+    # the kernel reduces in a tree.  Against float64 the kernel is within 2e-6.
+    x64 = x.astype(np.float64)
+    exact = x64 * w / np.sqrt(np.mean(x64 * x64) + 1e-5)
+    np.testing.assert_allclose(got, exact, rtol=2e-6, atol=0)
+    np.testing.assert_allclose(got, orc.rmsnorm(x, w), rtol=max(2e-6, 4 * np.sqrt(n) * 2.0 ** -24), atol=0)
     if n == 3:
         np.testing.assert_allclose(got, kat["rmsnorm"]["expected"], rtol=0, atol=kat["rmsnorm"]["tolerance"])
 
