@@ -199,6 +199,16 @@ tir_status tir_test_forward(tir_state *s, int32_t *out_id);
  * save_intermediate, src/forward.rs:287-308).  Enable before the forward. */
 tir_status tir_state_enable_dump(tir_state *s, int32_t enable);
 tir_status tir_state_dump(tir_state *s, float *out_host);
+/* Phase timeline (profiling; the reference's tracing is the debug-build
+ * save_intermediate, src/forward.rs:287-308): with step >= 0, every later
+ * launch records, for forward step `step`, eight values per phase per CTA:
+ * globaltimer stamps (ns) at start, inputs ready, input staged and release,
+ * then ns spent waiting for streamed weights, tiles processed, ns spent
+ * waiting for the previous phase, 0.  step < 0 turns it off.
+ * tir_state_trace copies n_phases x grid x 8 uint64 values. */
+tir_status tir_state_enable_trace(tir_state *s, int32_t step);
+tir_status tir_state_trace_dims(const tir_state *s, int32_t *n_phases, int32_t *grid);
+tir_status tir_state_trace(tir_state *s, uint64_t *out_host);
 
 /* ---- op-level kernels (device pointers, asynchronous on `stream`) --------- */
 

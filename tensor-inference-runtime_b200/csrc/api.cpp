@@ -43,21 +43,20 @@ static tir_status cuda_fail(cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(e_, what); \
     } while (0)
 
+// Rows per weight tile: the largest power of two (<= kMaxTileRows) whose
+// quants and scales fit one ring slot.
 static int tile_rows_max(int64_t k) {
     const int64_t per = k + scale_stride(k) * 2;
-    int64_t r = kStageBytes / per;
-    if (r > kMaxTileRows) r = kMaxTileRows;
-    return static_cast<int>(r) & ~1;
+    int r = kMaxTileRows;
+    while (r > 1 && r * per > kStageBytes) r >>= 1;
+    return r;
 }
 
+// With grid > 0, also no more rows than spread the matrix over every CTA.
 int tile_rows_for(int64_t k, int64_t n, int grid) {
     int r = tile_rows_max(k);
-    if (grid > 0) {
-        int64_t want = (n + grid - 1) / grid;
-        want = (want + 1) & ~int64_t(1);
-        if (want < 2) want = 2;
-        if (want < r) r = static_cast<int>(want);
-    }
+    if (grid > 0)
+        while (r > 1 && static_cast<int64_t>(r / 2) * grid >= n) r >>= 1;
     return r;
 }
 
@@ -129,7 +128,6 @@ tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_
     d.sk = static_cast<int32_t>(scale_stride(k));
     d.rows_per_tile = tile_rows_for(k, n, sms);
     d.n_tiles = static_cast<int32_t>((n + d.rows_per_tile - 1) / d.rows_per_tile);
-    d.segs = static_cast<int32_t>((k + kSegK - 1) / kSegK);
     d.wq = quants;
     d.ws = scales;
     d.in = x;
@@ -195,6 +193,8 @@ struct tir_state {
     int n_phases = 0;
     int32_t len = 0;
     bool dump_on = false;
+    unsigned long long* trace = nullptr;
+    int32_t trace_step = -1;
     int32_t* h_ids = nullptr;  // pinned, max_ctx
     uint32_t* h_err = nullptr; // pinned, 4
     ~tir_state() {
@@ -390,8 +390,10 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     if (!g->has_transformer) return fail(TIR_ERR_MISSING_FIELD, "Metadata Load error: missing required field: Layers");
     tir_transformer t = g->transformer;
     const uint64_t L = t.layers, H = t.embed_dim, hd = t.dim, nq = t.q_heads, nkv = t.k_v_heads;
+    // Fused pairs (RoPE, gate|up) need tiles of >= 2 rows: rows of H columns
+    // must fit twice in a ring slot.  A step has 5 phases per layer + 1.
     if (hd != static_cast<uint64_t>(kHeadDim) || nq == 0 || nkv == 0 || nq % nkv != 0 || H != nq * hd ||
-        H % 32 != 0 || H > 8192)
+        H % 32 != 0 || tile_rows_max(static_cast<int64_t>(H)) < 2 || 5 * t.layers + 1 > kMaxPhases)
         return fail(TIR_ERR_UNSUPPORTED_SHAPE,
                     "unsupported shape: head dim " + std::to_string(hd) + ", embedding " + std::to_string(H) +
                         ", heads " + std::to_string(nq) + "/" + std::to_string(nkv) + " (head dim must be 64)");
@@ -406,7 +408,7 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     if ((rc = need_tensor(g, "output.weight", TIR_DTYPE_Q8_0, {H, t.vocab}, &to)) != TIR_OK) return rc;
     if ((rc = need_tensor(g, "output_norm.weight", TIR_DTYPE_F32, {H}, &ton)) != TIR_OK) return rc;
     const uint64_t F = t.ffn_dim, V = t.vocab;
-    if (F == 0 || F % 32 != 0 || F > 8192 || V == 0 || V > (1u << 30))
+    if (F == 0 || F % 32 != 0 || F > static_cast<uint64_t>(kMaxK) || V == 0 || V > (1u << 30))
         return fail(TIR_ERR_UNSUPPORTED_SHAPE, "unsupported ffn/vocab size");
     struct LT {
         const TensorInfo *an, *q, *k, *v, *o, *fn, *gt, *up, *dn;
@@ -590,7 +592,6 @@ static tir_status build_phases(tir_state* s) {
         d.sk = static_cast<int32_t>(mt.sk);
         d.rows_per_tile = tile_rows_for(mt.k, mt.n, 0);
         d.n_tiles = static_cast<int32_t>((mt.n + d.rows_per_tile - 1) / d.rows_per_tile);
-        d.segs = static_cast<int32_t>((mt.k + kSegK - 1) / kSegK);
         d.wq = mt.q;
         d.ws = mt.s;
         d.in = in;
@@ -610,7 +611,7 @@ static tir_status build_phases(tir_state* s) {
         a.kc = q.kc;
         a.vc = q.vc;
         ph.push_back(a);
-        ph.push_back(gemv(m->o[l], static_cast<int>(l), IN_RAW, s->attn, nullptr, EPI_RESID, s->x));
+        ph.push_back(gemv(m->o[l], static_cast<int>(l), IN_ATTN, s->attn, nullptr, EPI_RESID, s->x));
         ph.push_back(gemv(m->gu[l], static_cast<int>(l), IN_X_NORM, s->x, m->ffn_norm[l], EPI_GU, s->h));
         PhaseDesc dn = gemv(m->down[l], static_cast<int>(l), IN_RAW, s->h, nullptr, EPI_RESID, s->x);
         dn.dump = 1;
@@ -668,7 +669,7 @@ tir_status tir_state_create(tir_model* m, int32_t max_ctx, tir_state** out) {
               alloc(cache_f * 4, reinterpret_cast<void**>(&s->kc)) && alloc(cache_f * 4, reinterpret_cast<void**>(&s->vc)) &&
               alloc(static_cast<size_t>(max_ctx) * 32 * 4, reinterpret_cast<void**>(&s->rope_cos)) &&
               alloc(static_cast<size_t>(max_ctx) * 32 * 4, reinterpret_cast<void**>(&s->rope_sin)) &&
-              alloc(static_cast<size_t>(t.k_v_heads) * ms * group * (kHeadDim + 2) * 4,
+              alloc(static_cast<size_t>(t.k_v_heads) * ms * group * kAttnRec * 4,
                     reinterpret_cast<void**>(&s->attn_part)) &&
               alloc(static_cast<size_t>(L) * t.k_v_heads * 4, reinterpret_cast<void**>(&s->attn_cnt)) &&
               alloc(16, reinterpret_cast<void**>(&s->error)) &&
@@ -756,6 +757,8 @@ static tir_status launch_steps(tir_state* s, int n_steps, int pos0, const float*
     p.argmax_part = s->argmax_part;
     p.error = s->error;
     p.timeout_ns = timeout_ns();
+    p.trace = s->trace_step >= 0 ? s->trace : nullptr;
+    p.trace_step = s->trace_step;
     CUDA_TRY(cudaMemsetAsync(s->counters, 0, static_cast<size_t>(s->n_phases) * 4, s->stream), "counter reset");
     CUDA_TRY(cudaMemsetAsync(s->error, 0, 16, s->stream), "error reset");
     CUDA_TRY(cudaMemsetAsync(s->attn_cnt, 0, static_cast<size_t>(t.layers) * t.k_v_heads * 4, s->stream),
@@ -919,6 +922,41 @@ tir_status tir_state_dump(tir_state* s, float* out_host) {
     return TIR_OK;
 }
 
+tir_status tir_state_enable_trace(tir_state* s, int32_t step) {
+    clear_error();
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    if (step >= 0 && !s->trace) {
+        void* p = nullptr;
+        const size_t bytes = static_cast<size_t>(s->n_phases) * s->grid * kTraceFields * 8;
+        CUDA_TRY(cudaMalloc(&p, bytes), "trace buffer");
+        s->allocs.push_back(p);
+        s->trace = static_cast<unsigned long long*>(p);
+        CUDA_TRY(cudaMemset(p, 0, bytes), "trace buffer");
+    }
+    s->trace_step = step < 0 ? -1 : step;
+    return TIR_OK;
+}
+
+tir_status tir_state_trace_dims(const tir_state* s, int32_t* n_phases, int32_t* grid) {
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (n_phases) *n_phases = s->n_phases;
+    if (grid) *grid = s->grid;
+    return TIR_OK;
+}
+
+tir_status tir_state_trace(tir_state* s, uint64_t* out_host) {
+    clear_error();
+    if (!s || !out_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (!s->trace) return fail(TIR_ERR_INVALID_ARG, "trace not enabled");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "trace readback");
+    CUDA_TRY(cudaMemcpy(out_host, s->trace, static_cast<size_t>(s->n_phases) * s->grid * kTraceFields * 8,
+                        cudaMemcpyDeviceToHost),
+             "trace readback");
+    return TIR_OK;
+}
+
 // ---------------------------------------------------------------------------
 // op-level entry points
 // ---------------------------------------------------------------------------
@@ -942,8 +980,8 @@ tir_status tir_q8_repack(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t
 tir_status tir_q8_matmul(const float* x, const uint8_t* quants, const uint16_t* scales, float* out, int64_t n,
                          int64_t k, void* stream) {
     clear_error();
-    if (n < 0 || k <= 0 || k % 32 != 0 || k > kMaxSegs * kSegK)
-        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "q8 matvec needs 0 < k <= 8192, k % 32 == 0");
+    if (n < 0 || k <= 0 || k % 32 != 0 || k > kMaxK)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "q8 matvec needs 0 < k <= " + std::to_string(kMaxK) + ", k % 32 == 0");
     if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
     return q8_matmul_stream(x, quants, scales, out, n, k, stream);
 }
@@ -997,8 +1035,8 @@ tir_status tir_swiglu(const float* x, const uint8_t* gate_q, const uint16_t* gat
                       const uint16_t* up_s, const uint8_t* down_q, const uint16_t* down_s, float* out, int64_t k,
                       int64_t f, void* stream) {
     clear_error();
-    if (k <= 0 || f <= 0 || k % 32 || f % 32 || k > 8192 || f > 8192)
-        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "swiglu needs k, f multiples of 32 and <= 8192");
+    if (k <= 0 || f <= 0 || k % 32 || f % 32 || k > kMaxK || f > kMaxK)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "swiglu needs k, f multiples of 32 and <= " + std::to_string(kMaxK));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* tmp = nullptr;
     CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&tmp), static_cast<size_t>(3 * f) * 4, st), "swiglu scratch");

@@ -141,6 +141,31 @@ __global__ void rope_kernel(float* __restrict__ q, int64_t nq, float* __restrict
     }
 }
 
+// f32 -> f16 bits, round to nearest even, in 32-bit integer arithmetic (the
+// rule of the `half` crate's f16::from_f32; NaN stays a quiet NaN).
+__device__ __forceinline__ uint32_t f32_to_f16_bits(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t exp = (x >> 23) & 0xffu;
+    const uint32_t man = x & 0x7fffffu;
+    if (exp == 0xffu) return sign | 0x7c00u | (man ? (0x200u | (man >> 13)) : 0u);
+    const int e = static_cast<int>(exp) - 127 + 15;
+    if (e >= 0x1f) return sign | 0x7c00u;
+    if (e <= 0) {
+        const int s = 14 - e;
+        if (s > 24) return sign;
+        const uint32_t m = man | 0x800000u;
+        uint32_t q = m >> s;
+        const uint32_t r = m & ((1u << s) - 1u), half = 1u << (s - 1);
+        if (r > half || (r == half && (q & 1u))) ++q;
+        return sign | q;
+    }
+    uint32_t h = sign | (static_cast<uint32_t>(e) << 10) | (man >> 13);
+    const uint32_t r = man & 0x1fffu;
+    if (r > 0x1000u || (r == 0x1000u && (h & 1u))) ++h;
+    return h;
+}
+
 // src/kernels.rs:8-31, one thread per 32-value block, bit-exact.
 __global__ void activated_q8_kernel(const float* __restrict__ x, int64_t nb, uint8_t* __restrict__ out) {
     for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < nb;
@@ -150,10 +175,10 @@ __global__ void activated_q8_kernel(const float* __restrict__ x, int64_t nb, uin
         for (int i = 1; i < 32; ++i)
             if (!(total_key(fabsf(pre[best])) > total_key(fabsf(pre[i])))) best = i;
         const float scale = __fdiv_rn(pre[best], 127.0f);
-        const uint16_t h = __half_as_ushort(__float2half_rn(scale));
+        const uint32_t h = f32_to_f16_bits(scale);
         uint8_t* post = out + b * 34;
-        post[0] = static_cast<uint8_t>(h & 0xff);
-        post[1] = static_cast<uint8_t>(h >> 8);
+        post[0] = static_cast<uint8_t>(h & 0xffu);
+        post[1] = static_cast<uint8_t>((h >> 8) & 0xffu);
         for (int i = 0; i < 32; ++i) post[2 + i] = static_cast<uint8_t>(f32_as_i8(roundf(__fdiv_rn(pre[i], scale))));
     }
 }

@@ -11,30 +11,33 @@
 // and finally LM (rmsnorm -> vocabulary matvec -> logits, argmax partials).
 // Each phase of each step is a grid-wide dependency: its CTAs start once every
 // CTA finished the previous phase (monotonic per-phase counters).  Weights never
-// depend on activations, so a producer warp streams every CTA's weight tiles
-// into a shared-memory ring with TMA bulk copies, across phase and step
-// boundaries, while the consumer warps wait on dependencies.
+// depend on activations, so every CTA streams its weight tiles into a
+// shared-memory ring with TMA bulk copies, across phase and step boundaries,
+// while its warps wait on dependencies.
 #pragma once
 #include <cstdint>
 
 namespace tir {
 
 // ---- launch geometry --------------------------------------------------------
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;  // + one producer warp
-constexpr int kStageBytes = 18432;               // one weight tile
-constexpr int kStages = 11;                      // ring depth
-constexpr int kMaxTileRows = 16;
-constexpr int kSegK = 512;                       // k-columns per warp segment
-constexpr int kMaxSegs = 16;                     // k <= 8192
-constexpr int kMaxSegsPerWarp = 2;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;            // one CTA of 8 warps per SM
+constexpr int kStageBytes = 9216;                // one weight tile (ring slot)
+constexpr int kStages = 21;                      // ring depth
+constexpr int kMaxTileRows = 8;                  // rows per tile: 1, 2, 4 or 8
+constexpr int kMaxK = 6144;                      // longest matvec row (columns)
+constexpr int kMaxPhases = 128;                  // phases per step (5 per layer + 1)
 constexpr int kHeadDim = 64;                     // attention head size supported
 constexpr int kAttnChunk = 32;                   // positions per attention chunk
-constexpr int kAttnHeadsPerPass = kConsumerWarps;
+constexpr int kAttnHeadsPerPass = kWarps;
 
 enum PhaseKind : int32_t { PH_GEMV = 0, PH_ATTN = 1 };
-enum InKind : int32_t { IN_RAW = 0, IN_X_NORM = 1, IN_X0_NORM = 2 };
+// IN_ATTN: the attention output, merged from the per-split partial softmaxes
+// by the reader when there are at most kReaderCombineMaxSplits splits.
+enum InKind : int32_t { IN_RAW = 0, IN_X_NORM = 1, IN_X0_NORM = 2, IN_ATTN = 3 };
+constexpr int kReaderCombineMaxSplits = 4;
+constexpr int kAttnRec = 68;     // floats per split record: max, sum, 2 pad, o[64]
+constexpr int kTraceFields = 8;  // per (phase, CTA): 4 stamps, data wait, tiles, dep wait, pad
 enum EpiKind : int32_t { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GU = 3, EPI_LOGITS = 4 };
 
 // Scale row stride (f16 elements) of the split Q8_0 layout: 16-byte rows.
@@ -43,9 +46,8 @@ __host__ __device__ constexpr int64_t scale_stride(int64_t k) { return ((k / 32)
 struct PhaseDesc {
     int32_t kind, layer, in_kind, epi;
     int32_t n, k, sk;          // rows, columns, scale stride (halves)
-    int32_t rows_per_tile, n_tiles, segs;
+    int32_t rows_per_tile, n_tiles;
     int32_t dump;              // EPI_RESID: also write the residual to the dump
-    int32_t pad_;
     const uint8_t* wq;         // quants [n][k], q + 128
     const uint16_t* ws;        // f16 scales [n][sk]
     const float* in;           // IN_RAW input / IN_X_NORM residual buffer
@@ -76,7 +78,7 @@ struct DecodeParams {
     float* dump;               // optional [(layers+1)][H]
     const float* rope_cos;     // [max_ctx][32]
     const float* rope_sin;
-    float* attn_part;          // [kv][max_splits][group][2 + 64]
+    float* attn_part;          // [kv][max_splits][group][kAttnRec]
     uint32_t* attn_cnt;        // [layers][kv]
     float* attn_out;           // [H]
     const float* q;            // [H] (written by EPI_QKV)
@@ -84,6 +86,12 @@ struct DecodeParams {
     unsigned long long* argmax_part;  // [grid]
     uint32_t* error;           // [0] code, [1] phase, [2] step
     unsigned long long timeout_ns;
+    // Phase timeline of step `trace_step` (globaltimer ns), NULL when off:
+    // trace[(phase * grid + cta) * kTraceFields + {0 start, 1 inputs ready,
+    // 2 staged, 3 released, 4 ns waiting for ring data, 5 tiles, 6 ns waiting
+    // for the previous phase}]
+    unsigned long long* trace;
+    int32_t trace_step;
 };
 
 // Host launchers (decode.cu).

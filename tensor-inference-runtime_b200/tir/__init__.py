@@ -101,6 +101,9 @@ SIGNATURES = {
     "tir_test_forward": (C.c_int, [_vp, _i32p]),
     "tir_state_enable_dump": (C.c_int, [_vp, C.c_int32]),
     "tir_state_dump": (C.c_int, [_vp, _f32p]),
+    "tir_state_enable_trace": (C.c_int, [_vp, C.c_int32]),
+    "tir_state_trace_dims": (C.c_int, [_vp, _i32p, _i32p]),
+    "tir_state_trace": (C.c_int, [_vp, C.POINTER(C.c_uint64)]),
     "tir_q8_scale_stride": (_i64, [_i64]),
     "tir_q8_repack": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "tir_q8_matmul": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
@@ -388,6 +391,18 @@ class State:
 
     def enable_dump(self, on=True):
         check(lib().tir_state_enable_dump(self._h, 1 if on else 0))
+
+    def enable_trace(self, step):
+        check(lib().tir_state_enable_trace(self._h, int(step)))
+
+    def trace(self):
+        """[n_phases, grid, 8]: stamps (ns) start/ready/staged/released, ns waiting
+        for ring data, tiles, ns waiting for the previous phase."""
+        n, g = C.c_int32(), C.c_int32()
+        check(lib().tir_state_trace_dims(self._h, C.byref(n), C.byref(g)))
+        out = np.zeros((n.value, g.value, 8), np.uint64)
+        check(lib().tir_state_trace(self._h, out.ctypes.data_as(C.POINTER(C.c_uint64))))
+        return out
 
     def dump(self):
         out = np.empty((self.layers + 1, self.embed_dim), np.float32)

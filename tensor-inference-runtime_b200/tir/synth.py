@@ -132,7 +132,7 @@ def write_gguf(path, cfg, seed=0):
         head += struct.pack("<IQ", dtype, offset)
         offset += -(-_nbytes(dtype, shape) // ALIGN) * ALIGN
     head += b"\0" * (-len(head) % ALIGN)
-    tmp = path + ".partial"
+    tmp = f"{path}.partial.{os.getpid()}"  # ranks writing the same file never share a temp
     with open(tmp, "wb") as f:
         f.write(head)
         for (name, dtype, shape), off in zip(specs, offsets):
