@@ -47,6 +47,9 @@ def parse_args(argv=None):
     ap.add_argument("--decode", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline", choices=["auto", "off"], default="auto")
+    ap.add_argument("--timeline", metavar="FILE.md", default=None,
+                    help="after the timed region, trace forward step 100 of one more generate "
+                         "and write the per-phase timeline summary to FILE.md")
     return ap.parse_args(argv)
 
 
@@ -301,6 +304,13 @@ def run_ours(args, dist):
     }
     if dist.rank == 0 and dist.world == 1 and args.cpu_baseline == "auto":
         line["cpu_baseline"] = cpu_baseline(args)
+    if args.timeline and dist.rank == 0:
+        from tir import timeline
+        st.enable_trace(min(100, n_fwd - 1))
+        st.generate_capped(prompt, args.decode)
+        st.enable_trace(-1)
+        with open(args.timeline, "w") as f:
+            f.write(timeline.to_markdown(timeline.summarize(st.trace())) + "\n")
     st.close()
     model.close()
     return line

@@ -475,7 +475,6 @@ __device__ __forceinline__ float warp_tile(const uint8_t* tq, const uint16_t* ts
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = 0.f;
-#pragma unroll(R == 1 ? 4 : (R == 2 ? 2 : 1))
     for (int c = lane; c < nchunks; c += 32) {
         float x[16];
 #pragma unroll
