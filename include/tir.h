@@ -241,6 +241,19 @@ void tir_rope_angles(float base, int64_t pos, int64_t dim, float *out_host);
 tir_status tir_swiglu(const float *x, const uint8_t *gate_q, const uint16_t *gate_s,
                       const uint8_t *up_q, const uint16_t *up_s, const uint8_t *down_q,
                       const uint16_t *down_s, float *out, int64_t k, int64_t f, void *stream);
+/* tir_swiglu without device allocation.  No counterpart in the reference (its
+ * swiglu, src/math.rs:164-178, allocates host Vecs per call); this is for
+ * callers that must not allocate device memory while they run.  Same inputs
+ * and results as tir_swiglu, but gate, up and silu(gate)*up live in a fixed
+ * per-device static array, so f <= 6144 (k <= 6144 as for tir_swiglu); larger
+ * sizes return TIR_ERR_UNSUPPORTED_SHAPE.  Makes no cudaMalloc/cudaFree call.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress)
+ * with that device current; make it before any stream capture on the device.
+ * Calls on the same device must not overlap in time: they share the array. */
+tir_status tir_swiglu_static(const float *x, const uint8_t *gate_q, const uint16_t *gate_s,
+                             const uint8_t *up_q, const uint16_t *up_s, const uint8_t *down_q,
+                             const uint16_t *down_s, float *out, int64_t k, int64_t f,
+                             void *stream);
 /* activated_q8 (src/kernels.rs:8-31): k floats -> k/32 Q8_0 blocks, bit-exact. */
 tir_status tir_activated_q8(const float *x, int64_t k, uint8_t *out_blocks, void *stream);
 /* q8_act_matmul (src/math.rs:101-112): quantised activation (Q8_0 blocks) x

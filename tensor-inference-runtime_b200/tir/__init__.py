@@ -114,6 +114,7 @@ SIGNATURES = {
     "tir_rope": (C.c_int, [_vp, _i64, _vp, _i64, _f32p, _i64, _vp]),
     "tir_rope_angles": (None, [C.c_float, _i64, _i64, _f32p]),
     "tir_swiglu": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "tir_swiglu_static": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_activated_q8": (C.c_int, [_vp, _i64, _vp, _vp]),
     "tir_q8_act_matmul": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_argmax": (C.c_int, [_vp, _i64, _vp, _vp]),
@@ -456,6 +457,13 @@ def swiglu(x, gate, up, down, out, k, f, stream=None):
     """gate/up/down: (quants, scales) pairs of split-layout matrices."""
     check(lib().tir_swiglu(_ptr(x), _ptr(gate[0]), _ptr(gate[1]), _ptr(up[0]), _ptr(up[1]),
                            _ptr(down[0]), _ptr(down[1]), _ptr(out), k, f, _stream(stream)))
+
+
+def swiglu_static(x, gate, up, down, out, k, f, stream=None):
+    """swiglu with its intermediates in a fixed per-device array (f <= 6144);
+    allocates no device memory.  Calls on one device must not overlap."""
+    check(lib().tir_swiglu_static(_ptr(x), _ptr(gate[0]), _ptr(gate[1]), _ptr(up[0]), _ptr(up[1]),
+                                  _ptr(down[0]), _ptr(down[1]), _ptr(out), k, f, _stream(stream)))
 
 
 def activated_q8(x, k, out_blocks, stream=None):
