@@ -47,6 +47,9 @@ def parse_args(argv=None):
     ap.add_argument("--decode", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline", choices=["auto", "off"], default="auto")
+    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
+                    help="decode: the batch-1 decode loop (default); gemv: the isolated Q8_0 GEMV sweep "
+                         "over the TinyLlama projection shapes")
     ap.add_argument("--timeline", metavar="FILE.md", default=None,
                     help="after the timed region, trace forward step 100 of one more generate "
                          "and write the per-phase timeline summary to FILE.md")
@@ -316,6 +319,70 @@ def run_ours(args, dist):
     return line
 
 
+GEMV_SHAPES = [(2048, 2048), (2048, 256), (2048, 5632), (5632, 2048), (2048, 32000)]  # (K, N)
+
+
+def run_gemv(args):
+    """Isolated Q8_0 GEMV sweep (batch 1) over the TinyLlama projection shapes:
+    x f32 N(0, 1), weights int8 uniform in [-127, 127] with f16 scales
+    |N(0, 0.02)| / 127, seeded, in the tile-major layout the decode kernel
+    streams; each launch reads the next of several weight copies (>= 4x the
+    126 MB L2 in total) so weights stream from HBM.  Value = weight bytes
+    (N K / 32 x 34) over the summed device time of all shapes."""
+    import torch
+
+    import tir
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    l2 = 126 * 2 ** 20
+    per_shape = []
+    tot_bytes, tot_ms = 0.0, 0.0
+    stream = torch.cuda.current_stream()
+    for k, n in GEMV_SHAPES:
+        nb = k // 32
+        wbytes = n * nb * 34
+        tiled = tir.q8_tiled_bytes(n, k)
+        copies = max(2, -(-4 * l2 // tiled))
+        ws = []
+        for _ in range(copies):
+            q = torch.randint(-127, 128, (n, nb, 32), dtype=torch.int8, device="cuda", generator=g)
+            sc = (torch.randn(n, nb, 1, device="cuda", generator=g).abs() * 0.02 / 127).half()
+            blocks = torch.cat([sc.view(torch.uint8), q.view(torch.uint8)], dim=2).contiguous()
+            w = torch.empty(tiled, dtype=torch.uint8, device="cuda")
+            tir.q8_repack_tiled(blocks, n, k, w)
+            ws.append(w)
+            del q, sc, blocks
+        x = torch.randn(k, device="cuda", generator=g)
+        out = torch.empty(n, device="cuda")
+        for i in range(max(args.warmup, 3) * copies):
+            tir.q8_matmul_tiled(x, ws[i % copies], out, n, k)
+        iters = max(args.steps, 1) * copies
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(iters):
+            tir.q8_matmul_tiled(x, ws[i % copies], out, n, k)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        per_shape.append({"k": k, "n": n, "us": ms * 1e3, "weight_gbs": wbytes / (ms / 1e3) / 1e9, "copies": copies})
+        tot_bytes += wbytes
+        tot_ms += ms
+        del ws
+    peak, peak_kind = peaks()
+    gbs = tot_bytes / (tot_ms / 1e3) / 1e9
+    line = {"metric": "Q8_0 GEMV weight GB/s (batch 1, TinyLlama projection shapes)", "value": gbs, "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded int8 weights, f16 scales, f32 activations)",
+            "config": {"workload": "Q8_0 GEMV sweep K->N: " + ", ".join(f"{k}->{n}" for k, n in GEMV_SHAPES),
+                       "l2": "each launch reads the next of >= 4x L2 of weight copies"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "traffic": None, "peak_kind": peak_kind},
+            "shapes": per_shape, "gpu_launches": sum(max(args.steps, 1) * s["copies"] for s in per_shape)}
+    print(json.dumps(line), flush=True)
+
+
 def main(argv=None):
     args = parse_args(argv)
     world = int(os.environ.get("WORLD_SIZE", 1))
@@ -323,6 +390,10 @@ def main(argv=None):
     if args.impl == "reference":
         if rank == 0:
             run_reference(args, None)
+        return 0
+    if args.workload == "gemv":
+        if rank == 0:
+            run_gemv(args)
         return 0
     dist = Dist("nccl")
     try:

@@ -213,11 +213,22 @@ tir_status tir_state_trace(tir_state *s, uint64_t *out_host);
 /* ---- op-level kernels (device pointers, asynchronous on `stream`) --------- */
 
 /* Q8_0 blocks (34 B: f16 scale LE + 32 int8) of a [rows][k] tensor into the
- * runtime's split layout: quants [rows][k] uint8 holding q+128, scales
+ * runtime's split layout: quants [rows][k] signed int8 q, scales
  * [rows][scale_stride] f16 with scale_stride = tir_q8_scale_stride(k). */
 int64_t tir_q8_scale_stride(int64_t k);
 tir_status tir_q8_repack(const uint8_t *blocks, int64_t rows, int64_t k, uint8_t *quants,
                          uint16_t *scales, void *stream);
+/* Tile-major Q8_0 layout (the layout the decode kernel streams): tiles of
+ * tir_q8_tile_rows(k) rows, each holding its rows' int8 quants followed by
+ * their f16 scales (scale_stride per row), so one bulk copy moves a tile.
+ * tir_q8_tiled_bytes gives the buffer size (-1 for an unsupported k). */
+int64_t tir_q8_tile_rows(int64_t k);
+int64_t tir_q8_tiled_bytes(int64_t n, int64_t k);
+tir_status tir_q8_repack_tiled(const uint8_t *blocks, int64_t rows, int64_t k, uint8_t *out,
+                               void *stream);
+/* q8_matmul (src/math.rs:87-98) over the tile-major layout. */
+tir_status tir_q8_matmul_tiled(const float *x, const uint8_t *w, float *out, int64_t n, int64_t k,
+                               void *stream);
 /* q8_matmul (src/math.rs:87-98): out[n] = sum_b f32(s[n,b]) * sum_i x[32b+i]*q[n,b,i].
  * Streaming sm_100a GEMV over the split layout. */
 tir_status tir_q8_matmul(const float *x, const uint8_t *quants, const uint16_t *scales,

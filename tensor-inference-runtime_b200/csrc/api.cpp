@@ -43,21 +43,13 @@ static tir_status cuda_fail(cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(e_, what); \
     } while (0)
 
-// Rows per weight tile: the largest power of two (<= kMaxTileRows) whose
-// quants and scales fit one ring slot.
-static int tile_rows_max(int64_t k) {
-    const int64_t per = k + scale_stride(k) * 2;
-    int r = kMaxTileRows;
-    while (r > 1 && r * per > kStageBytes) r >>= 1;
-    return r;
-}
-
-// With grid > 0, also no more rows than spread the matrix over every CTA.
-int tile_rows_for(int64_t k, int64_t n, int grid) {
-    int r = tile_rows_max(k);
-    if (grid > 0)
-        while (r > 1 && static_cast<int64_t>(r / 2) * grid >= n) r >>= 1;
-    return r;
+// Rows per weight tile of a matrix with k columns (gemv_tile_rows, even, so
+// fused pairs -- RoPE, gate|up -- never straddle tiles); 0 if k is not a
+// positive multiple of 32 or longer than kMaxK.
+int tile_rows_for(int64_t k, bool pairs) {
+    (void)pairs;
+    if (k <= 0 || k % 32 != 0 || k > kMaxK || gemv_wpr(k) > kWarps) return 0;
+    return gemv_tile_rows(k);
 }
 
 // rope_angles (src/math.rs:181-193) and cosf/sinf of each angle, exactly as
@@ -126,8 +118,9 @@ tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_
     d.n = static_cast<int32_t>(n);
     d.k = static_cast<int32_t>(k);
     d.sk = static_cast<int32_t>(scale_stride(k));
-    d.rows_per_tile = tile_rows_for(k, n, sms);
+    d.rows_per_tile = tile_rows_for(k, false);
     d.n_tiles = static_cast<int32_t>((n + d.rows_per_tile - 1) / d.rows_per_tile);
+    d.tiled = scales == nullptr ? 1 : 0;
     d.wq = quants;
     d.ws = scales;
     d.in = x;
@@ -152,10 +145,14 @@ using namespace tir;
 // ---------------------------------------------------------------------------
 // model / state objects
 // ---------------------------------------------------------------------------
+// A weight matrix in HBM: tile-major (q = the tiled matrix, s unused, r rows
+// per tile) for the streamed projections, split (q [n][k], s [n][sk]) for the
+// embedding table, which is read one row at a time.
 struct Mat {
     uint8_t* q = nullptr;
     uint16_t* s = nullptr;
-    int64_t n = 0, k = 0, sk = 0;
+    int64_t n = 0, k = 0, sk = 0, r = 0;
+    bool tiled = false;
 };
 
 struct tir_model {
@@ -390,10 +387,11 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     if (!g->has_transformer) return fail(TIR_ERR_MISSING_FIELD, "Metadata Load error: missing required field: Layers");
     tir_transformer t = g->transformer;
     const uint64_t L = t.layers, H = t.embed_dim, hd = t.dim, nq = t.q_heads, nkv = t.k_v_heads;
-    // Fused pairs (RoPE, gate|up) need tiles of >= 2 rows: rows of H columns
-    // must fit twice in a ring slot.  A step has 5 phases per layer + 1.
+    // Fused pairs (RoPE, gate|up) need tiles of an even number of rows of H
+    // columns that fit one ring slot.  A step has 5 phases per layer + 1.
     if (hd != static_cast<uint64_t>(kHeadDim) || nq == 0 || nkv == 0 || nq % nkv != 0 || H != nq * hd ||
-        H % 32 != 0 || tile_rows_max(static_cast<int64_t>(H)) < 2 || 5 * t.layers + 1 > kMaxPhases)
+        H % 32 != 0 || H > static_cast<uint64_t>(kMaxK) || tile_rows_for(static_cast<int64_t>(H), true) == 0 ||
+        5 * t.layers + 1 > kMaxPhases)
         return fail(TIR_ERR_UNSUPPORTED_SHAPE,
                     "unsupported shape: head dim " + std::to_string(hd) + ", embedding " + std::to_string(H) +
                         ", heads " + std::to_string(nq) + "/" + std::to_string(nkv) + " (head dim must be 64)");
@@ -438,7 +436,7 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     m->t = t;
     // Layout: one allocation; each matrix = quants then scales, 256-B aligned.
     size_t off = 0;
-    auto plan = [&](Mat& mt, int64_t n, int64_t k) {
+    auto plan = [&](Mat& mt, int64_t n, int64_t k) {  // split layout
         mt.n = n;
         mt.k = k;
         mt.sk = scale_stride(k);
@@ -446,6 +444,15 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
         off = a256(off + static_cast<size_t>(n * k));
         mt.s = reinterpret_cast<uint16_t*>(off);
         off = a256(off + static_cast<size_t>(n * mt.sk * 2));
+    };
+    auto plan_tiled = [&](Mat& mt, int64_t n, int64_t k, bool pairs) {
+        mt.n = n;
+        mt.k = k;
+        mt.sk = scale_stride(k);
+        mt.r = tile_rows_for(k, pairs);
+        mt.tiled = true;
+        mt.q = reinterpret_cast<uint8_t*>(off);
+        off = a256(off + static_cast<size_t>(q8_tiled_matrix_bytes(n, k)));
     };
     auto plan_f32 = [&](int64_t n) {
         const size_t at = off;
@@ -458,14 +465,14 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     m->down.resize(L);
     std::vector<size_t> an_off(L), fn_off(L);
     for (uint64_t l = 0; l < L; ++l) {
-        plan(m->qkv[l], static_cast<int64_t>(H + 2 * KVD), static_cast<int64_t>(H));
-        plan(m->o[l], static_cast<int64_t>(H), static_cast<int64_t>(H));
-        plan(m->gu[l], static_cast<int64_t>(2 * F), static_cast<int64_t>(H));
-        plan(m->down[l], static_cast<int64_t>(H), static_cast<int64_t>(F));
+        plan_tiled(m->qkv[l], static_cast<int64_t>(H + 2 * KVD), static_cast<int64_t>(H), true);
+        plan_tiled(m->o[l], static_cast<int64_t>(H), static_cast<int64_t>(H), false);
+        plan_tiled(m->gu[l], static_cast<int64_t>(2 * F), static_cast<int64_t>(H), true);
+        plan_tiled(m->down[l], static_cast<int64_t>(H), static_cast<int64_t>(F), false);
         an_off[l] = plan_f32(static_cast<int64_t>(H));
         fn_off[l] = plan_f32(static_cast<int64_t>(H));
     }
-    plan(m->lm, static_cast<int64_t>(V), static_cast<int64_t>(H));
+    plan_tiled(m->lm, static_cast<int64_t>(V), static_cast<int64_t>(H), false);
     plan(m->embd, static_cast<int64_t>(V), static_cast<int64_t>(H));
     const size_t on_off = plan_f32(static_cast<int64_t>(H));
     m->dev_bytes = off;
@@ -476,7 +483,7 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     }
     auto fix = [&](Mat& mt) {
         mt.q = m->dev + reinterpret_cast<size_t>(mt.q);
-        mt.s = reinterpret_cast<uint16_t*>(m->dev + reinterpret_cast<size_t>(mt.s));
+        mt.s = mt.tiled ? nullptr : reinterpret_cast<uint16_t*>(m->dev + reinterpret_cast<size_t>(mt.s));
     };
     for (uint64_t l = 0; l < L; ++l) {
         fix(m->qkv[l]);
@@ -512,8 +519,9 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
         const int64_t rows = static_cast<int64_t>(ti->shape[1]);
         cudaError_t er = cudaMemcpy(staging, ti->data, ti->data_bytes, cudaMemcpyHostToDevice);
         if (er != cudaSuccess) return er;
-        const int rc2 = launch_repack(staging, rows, k, mt.q + row0 * mt.k, mt.s + row0 * mt.sk, mt.sk, step, roff,
-                                      nullptr);
+        const int rc2 = mt.tiled ? launch_repack_tiled(staging, rows, k, mt.q, mt.n, mt.r, step, row0 + roff, nullptr)
+                                 : launch_repack(staging, rows, k, mt.q + row0 * mt.k, mt.s + row0 * mt.sk, mt.sk,
+                                                 step, roff, nullptr);
         if (rc2 != 0) return static_cast<cudaError_t>(rc2);
         return cudaDeviceSynchronize();
     };
@@ -590,10 +598,11 @@ static tir_status build_phases(tir_state* s) {
         d.n = static_cast<int32_t>(mt.n);
         d.k = static_cast<int32_t>(mt.k);
         d.sk = static_cast<int32_t>(mt.sk);
-        d.rows_per_tile = tile_rows_for(mt.k, mt.n, 0);
+        d.rows_per_tile = static_cast<int32_t>(mt.r);
         d.n_tiles = static_cast<int32_t>((mt.n + d.rows_per_tile - 1) / d.rows_per_tile);
+        d.tiled = 1;
         d.wq = mt.q;
-        d.ws = mt.s;
+        d.ws = nullptr;
         d.in = in;
         d.norm_w = norm_w;
         d.out = out;
@@ -983,7 +992,34 @@ tir_status tir_q8_matmul(const float* x, const uint8_t* quants, const uint16_t* 
     if (n < 0 || k <= 0 || k % 32 != 0 || k > kMaxK)
         return fail(TIR_ERR_UNSUPPORTED_SHAPE, "q8 matvec needs 0 < k <= " + std::to_string(kMaxK) + ", k % 32 == 0");
     if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
+    if (!quants || !scales) return fail(TIR_ERR_INVALID_ARG, "null weights");
     return q8_matmul_stream(x, quants, scales, out, n, k, stream);
+}
+
+int64_t tir_q8_tile_rows(int64_t k) { return tile_rows_for(k, false); }
+
+int64_t tir_q8_tiled_bytes(int64_t n, int64_t k) {
+    if (n < 0 || tile_rows_for(k, false) == 0) return -1;
+    return q8_tiled_matrix_bytes(n, k);
+}
+
+tir_status tir_q8_repack_tiled(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* out, void* stream) {
+    clear_error();
+    if (rows < 0 || k <= 0 || k % 32 != 0) return fail(TIR_ERR_BAD_QUANT_BLOCK, "q8_0 tensor length " + std::to_string(k) + " is not a multiple of 32");
+    const int r = tile_rows_for(k, false);
+    if (r == 0 || k > kMaxK) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "tiled layout needs k <= " + std::to_string(kMaxK));
+    if (rows > 0 && cudaMemsetAsync(out, 0, static_cast<size_t>(q8_tiled_matrix_bytes(rows, k)), static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return fail(TIR_ERR_CUDA, "tiled memset");
+    return op_rc(launch_repack_tiled(blocks, rows, k, out, rows, r, 1, 0, stream), "repack");
+}
+
+tir_status tir_q8_matmul_tiled(const float* x, const uint8_t* w, float* out, int64_t n, int64_t k, void* stream) {
+    clear_error();
+    if (n < 0 || k <= 0 || k % 32 != 0 || k > kMaxK)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "q8 matvec needs 0 < k <= " + std::to_string(kMaxK) + ", k % 32 == 0");
+    if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
+    if (!w) return fail(TIR_ERR_INVALID_ARG, "null weights");
+    return q8_matmul_stream(x, w, nullptr, out, n, k, stream);
 }
 
 tir_status tir_q8_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, void* stream) {

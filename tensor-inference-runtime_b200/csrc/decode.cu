@@ -2,25 +2,33 @@
 // (runtime.h): the batch-1 decode loop of src/forward.rs:13-258 /
 // src/lib.rs:239-314, or a single Q8_0 matvec (src/math.rs:87-98).
 //
-// One CTA of 8 warps per SM (cooperative launch: all CTAs co-resident).
+// One CTA of 12 warps per SM (cooperative launch: all CTAs co-resident).
 //
 // Weight stream.  Each CTA's weight tiles, in schedule order over every GEMV
-// phase of every step, flow through a kStages-deep shared-memory ring filled
-// by TMA bulk copies (cp.async.bulk, mbarrier completion).  Tile i sits in slot
-// i % kStages and is consumed by warp i % 8, which refills the slot with tile
-// i + kStages as soon as it is done.  Weights never wait for activations, so
-// HBM keeps streaming while the warps wait on phase dependencies.
+// phase of every step, are streamed warp by warp: the HBM layout keeps each
+// warp's slice of a tile contiguous (runtime.h q8_slice_offset), and every
+// warp copies its own slices with 16-byte cp.async into a private
+// kWarpSlots-deep shared-memory ring, kWarpSlots tiles ahead of the tile it is
+// computing.  No warp waits for another to free a slot, and no copy engine
+// serialises small copies.  Weights never wait for activations, so HBM keeps
+// streaming across phase boundaries while the warps wait on dependencies.
 //
 // Phases.  Every CTA waits (bounded) until all CTAs released the previous
-// phase, stages the phase input once into shared memory (rmsnorm fused), then
-// each warp works through its tiles independently -- row dots, one butterfly
-// reduction per tile, fused epilogue (RoPE + KV append, residual, SiLU*up,
-// logits + argmax) -- and the CTA releases the phase.
+// phase, stages the phase input once (rmsnorm fused) as per-block fixed-point
+// digits, then all warps work through the CTA's tiles together: thread (row
+// lane, column block b) owns block b of every row its row lane covers, keeps
+// block b of the input in registers for the whole phase, and leaves one
+// partial dot per (row, block); batches of up to 8 tiles are reduced with
+// shuffles and one CTA barrier, and the fused epilogue (RoPE + KV append,
+// residual, SiLU*up, logits + argmax) runs one thread per row.
 //
-// Q8_0 split layout: quants are stored as u = q + 128 (one byte), so a weight
-// becomes an exact f32 with one byte permute and one add:
-//   float(0x4B000000 | u) = 2^23 + u,   (2^23 + u) - (2^23 + 128) = q.
-// Products and sums use packed f32x2 FMA (sm_100).
+// Arithmetic.  Weights stay signed int8.  The input of each 32-column block is
+// encoded as integers q_i = round(x_i * 2^(22-E)), 2^E > max |x_i| of the
+// block, split into three signed base-256 digits (q = d0 + 256 d1 + 65536 d2),
+// so a block dot is three exact integer dp4a chains; the block's f16 weight
+// scale and 2^(E-22) are applied in f32.  The relative error of a row dot is
+// that of f32 accumulation (the fixed point keeps 22 bits below the block
+// maximum), well inside the path's f32 tolerance.
 //
 // Every wait is bounded by DecodeParams::timeout_ns (globaltimer); on expiry the
 // kernel records TIR_ERR_TIMEOUT, every CTA leaves at its next phase boundary,
@@ -40,14 +48,14 @@ namespace tir {
 constexpr uint32_t kErrTimeout = 25;   // TIR_ERR_TIMEOUT
 constexpr uint32_t kErrBadToken = 12;  // TIR_ERR_BAD_TOKEN
 constexpr uint32_t FULL = 0xffffffffu;
-constexpr uint32_t kBarAll = 1;  // named barrier id for the CTA's 8 warps
+constexpr uint32_t kBarAll = 1;  // named barrier id for the CTA's warps
 
 // Where the weight stream reads a phase's tiles (cached in shared memory so
 // refills need no global loads).
 struct TileSrc {
     const uint8_t* wq;
     const uint16_t* ws;
-    int32_t k, sk, n, rows;
+    int32_t k, sk, n, rows, tiled;
 };
 
 struct AttnBufs {
@@ -55,26 +63,40 @@ struct AttnBufs {
     float akv[2][kAttnChunk][kHeadDim];  // K and V rows of one chunk (TMA target)
 };
 
-struct __align__(128) Smem {
-    uint8_t ring[kStages][kStageBytes];  // weight tiles (TMA targets)
+// Staged GEMV input: per 32-column block, three words-of-digits planes (word j
+// of a plane holds the digit of columns 4j..4j+3) and the block's 2^(E-22);
+// before encoding, the merged attention output of an IN_ATTN phase passes
+// through xf (same storage, separated by a CTA barrier).
+struct StageBufs {
     union {
-        float xs[kMaxK];  // phase input, permuted [i4][chunk][4] (conflict-free 16-B reads)
+        float xf[kMaxK];
+        struct {
+            uint32_t xd[3][kMaxK / 32][8];
+            float xsc[kMaxK / 32];
+        };
+    };
+};
+
+struct __align__(128) Smem {
+    uint8_t ring[kWarps][kWarpSlots][kChunkBytes];  // per-warp weight slices (cp.async targets)
+    union {
+        StageBufs st;
         AttnBufs attn;
     } u;
-    uint64_t full[kStages];
     uint64_t abar;  // attention K/V copies
     TileSrc src[kMaxPhases];
+    float part[2][kWarps][8];  // per-warp row partials of a tile batch (double buffered)
     unsigned long long best[kWarps];
     float red[kWarps];
-    int32_t slot_issued[kStages];
     int16_t nmine[kMaxPhases], tfirst[kMaxPhases];
     int32_t token, phase_ok, abort_flag, attn_last, ok0;
 };
 
 // TMA bulk-copy destinations must start on 16-byte boundaries.
-static_assert(offsetof(Smem, ring) % 128 == 0 && kStageBytes % 128 == 0, "ring slots must be 16-byte aligned");
+static_assert(offsetof(Smem, ring) % 128 == 0 && kChunkBytes % 16 == 0, "ring slots must be 16-byte aligned");
 static_assert((offsetof(Smem, u) + offsetof(AttnBufs, akv)) % 16 == 0, "akv must be 16-byte aligned");
-static_assert(offsetof(Smem, full) % 8 == 0 && offsetof(Smem, abar) % 8 == 0, "mbarriers need 8-byte alignment");
+static_assert(offsetof(Smem, u) % 16 == 0, "staged digits are read as 16-byte vectors");
+static_assert(offsetof(Smem, abar) % 8 == 0, "mbarriers need 8-byte alignment");
 static_assert(sizeof(Smem) <= 227 * 1024, "shared memory budget");
 
 __device__ __forceinline__ const PhaseDesc& phase_at(const DecodeParams& p, int i) {
@@ -172,7 +194,7 @@ __device__ void build_schedule(const DecodeParams& p, Smem& s) {
         const int t0 = (static_cast<int>(blockIdx.x) - rot + G) % G;
         s.tfirst[ph] = static_cast<int16_t>(t0);
         s.nmine[ph] = static_cast<int16_t>(t0 < d.n_tiles ? (d.n_tiles - 1 - t0) / G + 1 : 0);
-        s.src[ph] = TileSrc{d.wq, d.ws, d.k, d.sk, d.n, d.rows_per_tile};
+        s.src[ph] = TileSrc{d.wq, d.ws, d.k, d.sk, d.n, d.rows_per_tile, d.tiled};
         rot = (rot + d.n_tiles) % G;
     }
 }
@@ -195,54 +217,126 @@ __device__ __forceinline__ bool pos_advance(const DecodeParams& p, const Smem& s
     return true;
 }
 
-// TMA copy of the tile at `c` (schedule index i) into slot i % kStages.
-__device__ __forceinline__ void issue_tile(Smem& s, const Pos& c, uint32_t i) {
-    const TileSrc& t = s.src[c.ph];
-    const int slot = static_cast<int>(i % kStages);
-    const int r0 = (s.tfirst[c.ph] + c.k * static_cast<int>(gridDim.x)) * t.rows;
-    const int rows = min(t.rows, t.n - r0);
-    const uint32_t bq = static_cast<uint32_t>(rows) * t.k;
-    const uint32_t bs = static_cast<uint32_t>(rows) * t.sk * 2u;
-    mbar_arrive_expect_tx(&s.full[slot], bq + bs);
-    bulk_g2s(s.ring[slot], t.wq + static_cast<size_t>(r0) * t.k, bq, &s.full[slot]);
-    bulk_g2s(s.ring[slot] + bq, t.ws + static_cast<size_t>(r0) * t.sk, bs, &s.full[slot]);
-    s.slot_issued[slot] += 1;
+// The warp's position in the CTA's tile schedule for its next copy, with the
+// copy geometry of that position's phase cached (recomputed only when the
+// cursor enters another phase): for the tile-major layout, the warp's slice in
+// the CTA's first tile of the phase and the stride to its next tile.
+struct Stream {
+    Pos c;
+    bool more;
+    int bound_ph;           // phase the cache below describes (-1: none)
+    const uint8_t* src0;    // tile-major: slice of tile tfirst
+    long long stride;       // tile-major: bytes between the CTA's tiles
+    int pieces;             // 16-byte pieces of the warp's slice (0: no slice)
+};
+
+__device__ __forceinline__ void stream_bind(const Smem& s, Stream& st, int warp) {
+    const TileSrc& t = s.src[st.c.ph];
+    const int wpr = gemv_wpr(t.k), RL = kWarps / wpr;
+    const int rl = warp / wpr, wi = warp % wpr;
+    st.bound_ph = st.c.ph;
+    st.pieces = 0;
+    if (rl < RL) {
+        const int nbw = q8_slice_blocks(t.k, wi), nbwp = (nbw + 7) / 8 * 8;
+        st.pieces = kTileMult * (nbw * 2 + nbwp / 8);
+        if (t.tiled) {
+            st.src0 = t.wq + q8_slice_offset(t.k, s.tfirst[st.c.ph], rl, wi);
+            st.stride = static_cast<long long>(gridDim.x) * q8_tile_bytes(t.k);
+        }
+    }
 }
 
-// Abort path (thread 0): wait, bounded, for the last copy issued into each slot.
-__device__ __forceinline__ void drain_ring(const DecodeParams& p, Smem& s) {
-    for (int slot = 0; slot < kStages; ++slot) {
-        const int n = *reinterpret_cast<volatile int32_t*>(&s.slot_issued[slot]);
-        if (n > 0) {
-            const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait(&s.full[slot], static_cast<uint32_t>(n - 1) & 1u) &&
-                   globaltimer_ns() - t0 < p.timeout_ns) {
+// Warp `warp` copies its slice of schedule tile i (position st.c, when
+// st.more) into its slot i % kWarpSlots with 16-byte cp.async (lane-strided,
+// coalesced) and commits one group -- an empty one past the schedule's end or
+// when the warp has no slice in that phase, so every thread's group count
+// stays in step with the tiles.  Slot layout: the slice's quants
+// (kTileMult rows x nbw blocks x 32 bytes), then its scales (kTileMult x nbwp
+// f16), for the tile-major and the split source layouts alike.
+__device__ __forceinline__ void issue_chunk(Smem& s, Stream& st, uint32_t i, int warp, int lane) {
+    if (st.more) {
+        if (st.bound_ph != st.c.ph) stream_bind(s, st, warp);
+        const TileSrc& t = s.src[st.c.ph];
+        uint8_t* dst = s.ring[warp][i % kWarpSlots];
+        if (t.tiled) {
+            const uint8_t* src = st.src0 + st.c.k * st.stride;
+            for (int pc = lane; pc < st.pieces; pc += 32) cp_async16(dst + 16 * pc, src + 16 * pc);
+        } else if (st.pieces > 0) {  // split layout (single-matrix launches)
+            const int wpr = gemv_wpr(t.k), RL = kWarps / wpr;
+            const int rl = warp / wpr, wi = warp % wpr;
+            const int ti = s.tfirst[st.c.ph] + st.c.k * static_cast<int>(gridDim.x);
+            const int nbw = q8_slice_blocks(t.k, wi), nbwp = (nbw + 7) / 8 * 8;
+            const int qpr = nbw * 2, spr = nbwp / 8;  // 16-byte pieces per row
+            const uint8_t* ws = reinterpret_cast<const uint8_t*>(t.ws);
+            for (int pc = lane; pc < st.pieces; pc += 32) {
+                const bool quant = pc < kTileMult * qpr;
+                const int pp = quant ? pc : pc - kTileMult * qpr;
+                const int per = quant ? qpr : spr;
+                const int j = pp / per, q = pp % per;
+                const int row = ti * t.rows + rl + RL * j;
+                if (row < t.n) {
+                    const uint8_t* src = quant ? t.wq + static_cast<size_t>(row) * t.k + 1024 * wi + 16 * q
+                                               : ws + static_cast<size_t>(row) * t.sk * 2 + 64 * wi + 16 * q;
+                    cp_async16(dst + 16 * pc, src);
+                }
             }
         }
     }
+    cp_async_commit();
+}
+
+// Issues the warp's next copy and moves its cursor one tile on.
+__device__ __forceinline__ void stream_next(const DecodeParams& p, Smem& s, Stream& st, uint32_t i, int warp,
+                                            int lane) {
+    issue_chunk(s, st, i, warp, lane);
+    if (st.more) st.more = pos_advance(p, s, st.c, 1);
 }
 
 // ---------------------------------------------------------------------------
 // GEMV phases
 // ---------------------------------------------------------------------------
 
-// 16 weights (one uint4 of u = q+128 bytes) dotted with 16 activations.
-__device__ __forceinline__ float dot16(const uint4 w, const float* x) {
-    const float2 magic = make_float2(-8388736.0f, -8388736.0f);
-    float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+// One thread's 32-column input block for a phase: digit planes of the half it
+// reads first (columns 16 fh .. 16 fh + 15) and second, and 2^(E-22).  The
+// half order fh = (b >> 2) & 1 spreads a warp's 16-byte shared-memory reads
+// of consecutive 32-byte blocks over all banks.
+struct XBlock {
+    uint32_t a[3][4], b[3][4];
+    float sc;
+};
+
+__device__ __forceinline__ void load_xblock(const Smem& s, int b, int fh, XBlock& x) {
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        const uint4 u = *reinterpret_cast<const uint4*>(&s.u.st.xd[d][b][4 * fh]);
+        const uint4 v = *reinterpret_cast<const uint4*>(&s.u.st.xd[d][b][4 * (fh ^ 1)]);
+        x.a[d][0] = u.x; x.a[d][1] = u.y; x.a[d][2] = u.z; x.a[d][3] = u.w;
+        x.b[d][0] = v.x; x.b[d][1] = v.y; x.b[d][2] = v.z; x.b[d][3] = v.w;
+    }
+    x.sc = s.u.st.xsc[b];
+}
+
+// Dot of one 32-weight block (signed int8, `q` = its first byte in shared
+// memory, `scale` its f16 scale) with the thread's input block:
+// sum_i q_i x_i = scale * 2^(E-22) * (S0 + 256 S1 + 65536 S2), S_d the exact
+// integer dot of the weights with digit plane d (|S_d| < 2^19).
+__device__ __forceinline__ float unit_dot(const uint8_t* q, uint16_t scale, const XBlock& x, int fh) {
+    const uint4 wa = *reinterpret_cast<const uint4*>(q + 16 * fh);
+    const uint4 wb = *reinterpret_cast<const uint4*>(q + 16 * (fh ^ 1));
+    const int A[4] = {static_cast<int>(wa.x), static_cast<int>(wa.y), static_cast<int>(wa.z), static_cast<int>(wa.w)};
+    const int B[4] = {static_cast<int>(wb.x), static_cast<int>(wb.y), static_cast<int>(wb.z), static_cast<int>(wb.w)};
+    int sa[3] = {0, 0, 0}, sb[3] = {0, 0, 0};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        float2 lo = make_float2(__uint_as_float(__byte_perm(ws[j], 0x4B000000u, 0x7440)),
-                                __uint_as_float(__byte_perm(ws[j], 0x4B000000u, 0x7441)));
-        float2 hi = make_float2(__uint_as_float(__byte_perm(ws[j], 0x4B000000u, 0x7442)),
-                                __uint_as_float(__byte_perm(ws[j], 0x4B000000u, 0x7443)));
-        lo = __fadd2_rn(lo, magic);
-        hi = __fadd2_rn(hi, magic);
-        a0 = __ffma2_rn(make_float2(x[4 * j], x[4 * j + 1]), lo, a0);
-        a1 = __ffma2_rn(make_float2(x[4 * j + 2], x[4 * j + 3]), hi, a1);
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            sa[d] = __dp4a(A[j], static_cast<int>(x.a[d][j]), sa[d]);
+            sb[d] = __dp4a(B[j], static_cast<int>(x.b[d][j]), sb[d]);
+        }
     }
-    return (a0.x + a0.y) + (a1.x + a1.y);
+    const int s0 = sa[0] + sb[0], s1 = sa[1] + sb[1], s2 = sa[2] + sb[2];
+    const float v = fmaf(static_cast<float>(s2), 65536.0f, static_cast<float>(s1 * 256 + s0));
+    return v * (__half2float(__ushort_as_half(scale)) * x.sc);
 }
 
 struct StepCtx {
@@ -260,10 +354,9 @@ __device__ __forceinline__ int attn_splits(const DecodeParams& p, int n_ctx) {
 
 // Sixteen consecutive input elements [k0, k0 + 16) (k0 % 16 == 0) in one
 // round trip: the step input x0 (explicit vector, or the embedding row of the
-// step's token, src/tokenizer.rs:10-32: f32(q) * f32(scale), exact), the
-// attention output (merging the per-split partial softmaxes when the
-// attention phase left that to its readers), or the phase's input buffer.
-// Data written by other CTAs is read from L2 (never a stale L1 line).
+// step's token, src/tokenizer.rs:10-32: f32(q) * f32(scale), exact) or the
+// phase's input buffer.  Data written by other CTAs is read from L2 (never a
+// stale L1 line).
 __device__ __forceinline__ void load16(const DecodeParams& p, const PhaseDesc& d, const StepCtx& st, int k0,
                                        float* v) {
     if (d.in_kind == IN_X0_NORM && !st.x0_given) {
@@ -275,47 +368,7 @@ __device__ __forceinline__ void load16(const DecodeParams& p, const PhaseDesc& d
         for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int b = 0; b < 4; ++b)
-                v[4 * j + b] = __fmul_rn(static_cast<float>(static_cast<int>((w[j] >> (8 * b)) & 0xffu) - 128), sc);
-    } else if (d.in_kind == IN_ATTN && st.S <= kReaderCombineMaxSplits) {
-        // softmax-weighted merge of the splits of head h = k0 / 64
-        const int h = k0 / kHeadDim, d0 = k0 % kHeadDim;
-        const int g = h / p.group, hh = h % p.group;
-        float4 ml[kReaderCombineMaxSplits];
-        float4 o[kReaderCombineMaxSplits][4];
-#pragma unroll
-        for (int j = 0; j < kReaderCombineMaxSplits; ++j) {
-            if (j < st.S) {
-                const float* rec =
-                    p.attn_part + ((static_cast<size_t>(g) * p.max_splits + j) * p.group + hh) * kAttnRec;
-                ml[j] = __ldcg(reinterpret_cast<const float4*>(rec));
-#pragma unroll
-                for (int q = 0; q < 4; ++q) o[j][q] = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d0) + q);
-            }
-        }
-        float M = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < kReaderCombineMaxSplits; ++j)
-            if (j < st.S) M = fmaxf(M, ml[j].x);
-        float L = 0.f, acc[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-#pragma unroll
-        for (int j = 0; j < kReaderCombineMaxSplits; ++j) {
-            if (j < st.S) {
-                const float w = expf(ml[j].x - M);
-                L = fmaf(ml[j].y, w, L);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    acc[4 * q] = fmaf(o[j][q].x, w, acc[4 * q]);
-                    acc[4 * q + 1] = fmaf(o[j][q].y, w, acc[4 * q + 1]);
-                    acc[4 * q + 2] = fmaf(o[j][q].z, w, acc[4 * q + 2]);
-                    acc[4 * q + 3] = fmaf(o[j][q].w, w, acc[4 * q + 3]);
-                }
-            }
-        }
-        const float inv = 1.0f / L;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = acc[i] * inv;
+                v[4 * j + b] = __fmul_rn(static_cast<float>(static_cast<int8_t>((w[j] >> (8 * b)) & 0xffu)), sc);
     } else {
         const float* src = d.in_kind == IN_X0_NORM ? p.x0 : d.in;
         const float4* s4 = reinterpret_cast<const float4*>(src + k0);
@@ -330,15 +383,55 @@ __device__ __forceinline__ void load16(const DecodeParams& p, const PhaseDesc& d
     }
 }
 
-// Each thread stages chunks c = tid and tid + 256 (16 columns each).
-constexpr int kChunksPerThread = (kMaxK / 16 + kThreads - 1) / kThreads;
+// Eight attention-output elements [k0, k0 + 8) of head h = k0 / 64, merged
+// from the S <= kReaderCombineMaxSplits per-split partial softmaxes the
+// attention phase left (max m_j, sum l_j, unnormalised o_j): one round trip.
+__device__ __forceinline__ void merge8(const DecodeParams& p, const StepCtx& st, int k0, float* v) {
+    const int h = k0 / kHeadDim, d0 = k0 % kHeadDim;
+    const int g = h / p.group, hh = h % p.group;
+    float2 ml[kReaderCombineMaxSplits];
+    float4 o[kReaderCombineMaxSplits][2];
+#pragma unroll
+    for (int j = 0; j < kReaderCombineMaxSplits; ++j) {
+        if (j < st.S) {
+            const float* rec = p.attn_part + ((static_cast<size_t>(g) * p.max_splits + j) * p.group + hh) * kAttnRec;
+            ml[j] = __ldcg(reinterpret_cast<const float2*>(rec));
+            o[j][0] = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d0));
+            o[j][1] = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d0) + 1);
+        }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kReaderCombineMaxSplits; ++j)
+        if (j < st.S) M = fmaxf(M, ml[j].x);
+    float L = 0.f, acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kReaderCombineMaxSplits; ++j) {
+        if (j < st.S) {
+            const float w = expf(ml[j].x - M);
+            L = fmaf(ml[j].y, w, L);
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                acc[4 * q] = fmaf(o[j][q].x, w, acc[4 * q]);
+                acc[4 * q + 1] = fmaf(o[j][q].y, w, acc[4 * q + 1]);
+                acc[4 * q + 2] = fmaf(o[j][q].z, w, acc[4 * q + 2]);
+                acc[4 * q + 3] = fmaf(o[j][q].w, w, acc[4 * q + 3]);
+            }
+        }
+    }
+    const float inv = 1.0f / L;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = acc[i] * inv;
+}
 
 // Operands of a phase that do not depend on the previous phase, loaded before
-// the dependency wait so their HBM latency hides behind it: the rmsnorm
-// weights of this thread's chunks and the position's RoPE cos/sin (lane i
-// holds pair i).
+// the dependency wait so their latency hides behind it: the rmsnorm weights of
+// this thread's 16-column chunk and the position's RoPE cos/sin (lane i holds
+// pair i).
 struct Prefetch {
-    float wr[kChunksPerThread * 16];
+    float wr[16];
     float rc, rs;
 };
 
@@ -346,23 +439,20 @@ __device__ __forceinline__ void prefetch_operands(const DecodeParams& p, const P
                                                   Prefetch& pf) {
     const int tid = threadIdx.x, lane = tid & 31;
     const bool norm = d.in_kind == IN_X_NORM || d.in_kind == IN_X0_NORM;
+    const int k0 = tid * 16;
+    if (norm && k0 < d.k) {
+        const float4* w4 = reinterpret_cast<const float4*>(d.norm_w + k0);
 #pragma unroll
-    for (int ci = 0; ci < kChunksPerThread; ++ci) {
-        const int k0 = (tid + ci * kThreads) * 16;
-        if (norm && k0 < d.k) {
-            const float4* w4 = reinterpret_cast<const float4*>(d.norm_w + k0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 t = __ldg(w4 + j);
-                pf.wr[ci * 16 + 4 * j] = t.x;
-                pf.wr[ci * 16 + 4 * j + 1] = t.y;
-                pf.wr[ci * 16 + 4 * j + 2] = t.z;
-                pf.wr[ci * 16 + 4 * j + 3] = t.w;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pf.wr[ci * 16 + i] = 0.f;
+        for (int j = 0; j < 4; ++j) {
+            const float4 t = __ldg(w4 + j);
+            pf.wr[4 * j] = t.x;
+            pf.wr[4 * j + 1] = t.y;
+            pf.wr[4 * j + 2] = t.z;
+            pf.wr[4 * j + 3] = t.w;
         }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pf.wr[i] = 1.0f;
     }
     pf.rc = 0.f;
     pf.rs = 0.f;
@@ -372,50 +462,77 @@ __device__ __forceinline__ void prefetch_operands(const DecodeParams& p, const P
     }
 }
 
-// Stages the phase input into s.u.xs (layout [i4][chunk][4], i.e. element
-// 16c + 4q + j at ((q * nchunks) + c) * 4 + j), with rmsnorm applied for
-// IN_*_NORM phases (src/math.rs:141-150: x*w / sqrt(sum(x^2)/n + eps); the
-// division is a multiplication by the correctly rounded reciprocal).  One
-// round trip of loads; for the step input, the CTA owning a chunk also
-// materialises it as the residual stream x (and dump row 0).
+// Four encoded values u (bytes 0..2 = digits + 128) -> the three digit words
+// (byte e of word d = digit d of value e, as signed int8).
+__device__ __forceinline__ void pack_digits(const uint32_t* u, uint32_t& w0, uint32_t& w1, uint32_t& w2) {
+    const uint32_t p01 = __byte_perm(u[0], u[1], 0x5140), p23 = __byte_perm(u[2], u[3], 0x5140);
+    const uint32_t q01 = __byte_perm(u[0], u[1], 0x0062), q23 = __byte_perm(u[2], u[3], 0x0062);
+    w0 = __byte_perm(p01, p23, 0x5410) ^ 0x80808080u;
+    w1 = __byte_perm(p01, p23, 0x7632) ^ 0x80808080u;
+    w2 = __byte_perm(q01, q23, 0x5410) ^ 0x80808080u;
+}
+
+// Stages the phase input for the GEMV threads.  Thread t loads columns
+// [16t, 16t + 16) (one round trip of loads), applies rmsnorm for IN_*_NORM
+// phases (src/math.rs:141-150: x*w / sqrt(sum(x^2)/n + eps), the division as
+// a multiplication by the correctly rounded reciprocal), and encodes its half
+// of the 32-column block as fixed point: with m = max |value| of the block
+// (the two halves sit in lanes t, t^1) and E = the exponent with
+// 2^(E-1) <= m < 2^E, q = round(value * 2^(22-E)) so |q| <= 2^22;
+// fma(value, 2^(22-E), 1.5 * 2^23) has q in its low mantissa bits, and adding
+// 0x408080 leaves u = q + 0x808080 in bytes 0..2, i.e. digit + 128 per byte
+// (q = d0 + 256 d1 + 65536 d2, |d2| <= 64).  Blocks with m < 2^-86 use E = -86.
+// For the step input, the CTA owning a chunk also materialises it as the
+// residual stream x (and dump row 0).
 __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
                                             const Prefetch& pf) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = d.k, nchunks = K / 16;
     const bool norm = d.in_kind == IN_X_NORM || d.in_kind == IN_X0_NORM;
-    float v[kChunksPerThread * 16];
+    const int c = tid;
+    float v[16];
 #pragma unroll
-    for (int ci = 0; ci < kChunksPerThread; ++ci) {
-        const int c = tid + ci * kThreads;
-        if (c < nchunks) {
-            load16(p, d, st, c * 16, v + ci * 16);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[ci * 16 + i] = 0.f;
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
+    if (d.in_kind == IN_ATTN && st.S <= kReaderCombineMaxSplits) {
+        // merge the attention splits 8 columns per thread, then regroup
+        for (int c8 = tid; c8 < K / 8; c8 += kThreads) {
+            float m[8];
+            merge8(p, st, c8 * 8, m);
+            float4* xf4 = reinterpret_cast<float4*>(s.u.st.xf + c8 * 8);
+            xf4[0] = make_float4(m[0], m[1], m[2], m[3]);
+            xf4[1] = make_float4(m[4], m[5], m[6], m[7]);
         }
-    }
-    if (d.in_kind == IN_X0_NORM) {
+        cbar();
+        if (c < nchunks) {
+            const float4* xf4 = reinterpret_cast<const float4*>(s.u.st.xf + c * 16);
 #pragma unroll
-        for (int ci = 0; ci < kChunksPerThread; ++ci) {
-            const int c = tid + ci * kThreads;
-            if (c < nchunks && c % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x)) {
-                float4* x4 = reinterpret_cast<float4*>(p.x + c * 16);
-                float4* d4 = p.dump ? reinterpret_cast<float4*>(p.dump + c * 16) : nullptr;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float4 t = make_float4(v[ci * 16 + 4 * j], v[ci * 16 + 4 * j + 1], v[ci * 16 + 4 * j + 2],
-                                                 v[ci * 16 + 4 * j + 3]);
-                    x4[j] = t;
-                    if (d4) d4[j] = t;
-                }
+            for (int q = 0; q < 4; ++q) {
+                const float4 t = xf4[q];
+                v[4 * q] = t.x;
+                v[4 * q + 1] = t.y;
+                v[4 * q + 2] = t.z;
+                v[4 * q + 3] = t.w;
             }
+        }
+        cbar();  // xf is read before the digits (same storage) are written
+    } else if (c < nchunks) {
+        load16(p, d, st, c * 16, v);
+    }
+    if (d.in_kind == IN_X0_NORM && c < nchunks && c % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x)) {
+        float4* x4 = reinterpret_cast<float4*>(p.x + c * 16);
+        float4* d4 = p.dump ? reinterpret_cast<float4*>(p.dump + c * 16) : nullptr;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 t = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            x4[j] = t;
+            if (d4) d4[j] = t;
         }
     }
     float inv = 1.0f;
     if (norm) {
         float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < kChunksPerThread * 16; ++i) ss = fmaf(v[i], v[i], ss);
+        for (int i = 0; i < 16; ++i) ss = fmaf(v[i], v[i], ss);
         ss = warp_sum(ss);
         if (lane == 0) s.red[warp] = ss;
         cbar();
@@ -423,26 +540,30 @@ __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, cons
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) total += s.red[w];
         inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), p.rms_eps)));
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], pf.wr[i]);
     }
-    float4* xs4 = reinterpret_cast<float4*>(s.u.xs);
+    float mx = 0.f;
 #pragma unroll
-    for (int ci = 0; ci < kChunksPerThread; ++ci) {
-        const int c = tid + ci * kThreads;
-        if (c < nchunks) {
+    for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, 1));
+    uint32_t ex = __float_as_uint(__fmul_rn(mx, inv)) >> 23;  // biased exponent of m
+    ex = max(ex, 40u);
+    const float up = __uint_as_float((275u - ex) << 23);    // 2^(22-E), E = ex - 126
+    const float down = __uint_as_float((ex - 21u) << 23);   // 2^(E-22)
+    const float mul = inv * up;                             // exact: power-of-two scaling
+    if (c < nchunks) {
+        uint32_t u[16];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float4 t;
-                const float* e = v + ci * 16 + 4 * q;
-                const float* w = pf.wr + ci * 16 + 4 * q;
-                if (norm) {
-                    t = make_float4(__fmul_rn(__fmul_rn(e[0], w[0]), inv), __fmul_rn(__fmul_rn(e[1], w[1]), inv),
-                                    __fmul_rn(__fmul_rn(e[2], w[2]), inv), __fmul_rn(__fmul_rn(e[3], w[3]), inv));
-                } else {
-                    t = make_float4(e[0], e[1], e[2], e[3]);
-                }
-                xs4[q * nchunks + c] = t;
-            }
-        }
+        for (int i = 0; i < 16; ++i) u[i] = __float_as_uint(fmaf(v[i], mul, 12582912.0f)) + 0x408080u;
+        const int b = c >> 1, h = c & 1;
+        uint32_t w[3][4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) pack_digits(u + 4 * g, w[0][g], w[1][g], w[2][g]);
+#pragma unroll
+        for (int dd = 0; dd < 3; ++dd)
+            *reinterpret_cast<uint4*>(&s.u.st.xd[dd][b][4 * h]) = make_uint4(w[dd][0], w[dd][1], w[dd][2], w[dd][3]);
+        if (h == 0) s.u.st.xsc[b] = down;
     }
     cbar();
 }
@@ -463,62 +584,18 @@ __device__ __forceinline__ float reduce8(const float* v, int lane) {
     return w;
 }
 
-// One warp, one tile of `rows` (<= R) rows: per-lane partial dots over the
-// lane's 16-column chunks (every 32nd), then the warp reduction.  Returns, in
-// lane l, the dot of row (l >> 2) & 7 (R > 1) or of row 0 (R == 1).
-template <int R>
-__device__ __forceinline__ float warp_tile(const uint8_t* tq, const uint16_t* ts, const float* xs, int K, int sk,
-                                           int rows) {
-    const int lane = threadIdx.x & 31;
-    const int nchunks = K / 16;
-    const float4* xv = reinterpret_cast<const float4*>(xs);
-    float acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.f;
-    for (int c = lane; c < nchunks; c += 32) {
-        float x[16];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const float4 t = xv[q * nchunks + c];
-            x[4 * q] = t.x;
-            x[4 * q + 1] = t.y;
-            x[4 * q + 2] = t.z;
-            x[4 * q + 3] = t.w;
-        }
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            if (r < rows) {
-                const uint4 w = *reinterpret_cast<const uint4*>(tq + static_cast<size_t>(r) * K + c * 16);
-                const float sc = __half2float(__ushort_as_half(ts[r * sk + (c >> 1)]));
-                acc[r] = fmaf(dot16(w, x), sc, acc[r]);
-            }
-        }
-    }
-    if constexpr (R == 1) {
-        return warp_sum(acc[0]);
-    } else {
-        float v[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = r < R ? acc[r < R ? r : 0] : 0.f;
-        return reduce8(v, lane);
-    }
-}
+// Trace accumulators of the traced step (thread 0 only).
+struct TraceAcc {
+    bool on;
+    unsigned long long data_wait_ns, dep_wait_ns, tiles;
+};
 
-// Fused epilogue of one tile, run by the lanes l with (l & 3) == 0: row
-// (l >> 2) & 7 of the tile (only lane 0 when R == 1); y = row dot, pre =
-// prefetched residual (EPI_RESID), (rc, rs) = the warp's RoPE cos/sin row
-// (lane i holds pair i).
-__device__ __forceinline__ void epilogue(const DecodeParams& p, const PhaseDesc& d, const StepCtx& st, int r0,
-                                         int rows, int R, float y, float pre, float rc, float rs,
+// Fused epilogue of matrix row n (or of the pair n, n + 1 for EPI_QKV / EPI_GU,
+// n even): y (y1) = the row dot(s), pre = prefetched residual (EPI_RESID),
+// (c, sn) = RoPE cos/sin of the pair.
+__device__ __forceinline__ void epilogue(const DecodeParams& p, const PhaseDesc& d, const StepCtx& st, int n,
+                                         float y, float y1, float pre, float c, float sn,
                                          unsigned long long& best) {
-    const int lane = threadIdx.x & 31;
-    const int row = R == 1 ? 0 : (lane >> 2) & 7;
-    const int n = r0 + row;
-    const float y1 = __shfl_down_sync(FULL, y, 4);  // row + 1 (pairs need R >= 2)
-    const int pair = (n % kHeadDim) >> 1;
-    const float c = __shfl_sync(FULL, rc, pair & 31);
-    const float sn = __shfl_sync(FULL, rs, pair & 31);
-    if ((lane & 3) != 0 || row >= rows || (R == 1 && lane != 0)) return;
     switch (d.epi) {
         case EPI_STORE:
             d.out[n] = y;
@@ -533,97 +610,147 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const PhaseDesc&
             if (d.dump && p.dump) p.dump[static_cast<size_t>(d.layer + 1) * p.H + n] = x;
             break;
         }
-        case EPI_GU:  // rows (2i, 2i+1) = (gate_i, up_i); src/math.rs:171-175
-            if ((row & 1) == 0) {
-                const float silu = __fdiv_rn(y, __fadd_rn(1.0f, expf(-y)));
-                d.out[n >> 1] = __fmul_rn(silu, y1);
-            }
+        case EPI_GU: {  // rows (2i, 2i+1) = (gate_i, up_i); src/math.rs:171-175
+            const float silu = __fdiv_rn(y, __fadd_rn(1.0f, expf(-y)));
+            d.out[n >> 1] = __fmul_rn(silu, y1);
             break;
-        case EPI_QKV:
-            if ((row & 1) == 0) {
-                // RoPE on adjacent pairs (src/math.rs:196-228), then q or the
-                // KV-cache append (src/forward.rs:71, :83-84).
-                const int H = p.H, kvd = p.kvd;
-                int idx = n;
-                float* dst;
-                bool rope = true;
-                if (idx < H) {
-                    dst = d.out + idx;
-                } else if (idx < H + kvd) {
-                    idx -= H;
-                    dst = d.kc + (static_cast<size_t>(idx / kHeadDim) * p.max_ctx + st.pos) * kHeadDim + idx % kHeadDim;
-                } else {
-                    idx -= H + kvd;
-                    dst = d.vc + (static_cast<size_t>(idx / kHeadDim) * p.max_ctx + st.pos) * kHeadDim + idx % kHeadDim;
-                    rope = false;
-                }
-                float e0 = y, e1 = y1;
-                if (rope) {
-                    e0 = __fadd_rn(__fmul_rn(c, y), __fmul_rn(-sn, y1));
-                    e1 = __fadd_rn(__fmul_rn(sn, y), __fmul_rn(c, y1));
-                }
-                dst[0] = e0;
-                dst[1] = e1;
+        }
+        case EPI_QKV: {
+            // RoPE on adjacent pairs (src/math.rs:196-228), then q or the
+            // KV-cache append (src/forward.rs:71, :83-84).
+            const int H = p.H, kvd = p.kvd;
+            int idx = n;
+            float* dst;
+            bool rope = true;
+            if (idx < H) {
+                dst = d.out + idx;
+            } else if (idx < H + kvd) {
+                idx -= H;
+                dst = d.kc + (static_cast<size_t>(idx / kHeadDim) * p.max_ctx + st.pos) * kHeadDim + idx % kHeadDim;
+            } else {
+                idx -= H + kvd;
+                dst = d.vc + (static_cast<size_t>(idx / kHeadDim) * p.max_ctx + st.pos) * kHeadDim + idx % kHeadDim;
+                rope = false;
             }
+            float e0 = y, e1 = y1;
+            if (rope) {
+                e0 = __fadd_rn(__fmul_rn(c, y), __fmul_rn(-sn, y1));
+                e1 = __fadd_rn(__fmul_rn(sn, y), __fmul_rn(c, y1));
+            }
+            dst[0] = e0;
+            dst[1] = e1;
             break;
+        }
         default:
             break;
     }
 }
 
-// Trace accumulators of the traced step (thread 0 only).
-struct TraceAcc {
-    bool on;
-    unsigned long long data_wait_ns, dep_wait_ns, tiles;
-};
-
-// The warp's tiles of one GEMV phase: schedule indices gidx + k for the
-// phase's ordinals k with (gidx + k) % 8 == warp.  Returns false on timeout.
-template <int R>
-__device__ __forceinline__ bool gemv_tiles(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
-                                           int ph, uint32_t gidx, const Prefetch& pf, TraceAcc& tr,
-                                           unsigned long long& best) {
+// The CTA's tiles of one GEMV phase (schedule indices gidx + k, k < nmine),
+// M units per thread per tile.  Batches of 8 / M tiles: every warp waits for
+// its own slices of the batch's tiles (cp.async groups), computes all their
+// units, and issues the copies kWarpSlots tiles ahead into the freed slots; the per-thread
+// partials are reduced over each warp (reduce8) into s.part, and after one CTA
+// barrier thread e runs the epilogue of batch row e, summing the partials of
+// the row lane's warps in order (deterministic).
+template <int M>
+__device__ __forceinline__ bool gemv_tiles(const DecodeParams& p, Smem& s, Stream& sw, const PhaseDesc& d,
+                                           const StepCtx& st, int ph, uint32_t gidx, const Prefetch& pf,
+                                           TraceAcc& tr, unsigned long long& best) {
+    static_assert(M == kTileMult, "tiles hold kTileMult rows per row lane");
+    constexpr int TB = 8 / M;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nm = s.nmine[ph];
     const int G = gridDim.x;
-    const int K = d.k, SK = d.sk, N = d.n;
-    int k = (warp - static_cast<int>(gidx % kWarps) + kWarps) % kWarps;
-    for (; k < nm; k += kWarps) {
-        const uint32_t i = gidx + static_cast<uint32_t>(k);
-        const int slot = static_cast<int>(i % kStages);
-        const int r0 = (s.tfirst[ph] + k * G) * R;
-        const int rows = min(R, N - r0);
-        const int row = R == 1 ? 0 : (lane >> 2) & 7;
+    const int K = d.k, N = d.n, R = d.rows_per_tile;
+    const int wpr = gemv_wpr(K), RL = kWarps / wpr;
+    const int rl = warp / wpr, wi = warp % wpr, b = wi * 32 + lane;
+    const int nbw = q8_slice_blocks(K, wi), nbwp = (nbw + 7) / 8 * 8;
+    const bool warp_on = rl < RL;
+    const bool lane_on = warp_on && lane < nbw;
+    const int fh = (b >> 2) & 1;
+    const int nm = s.nmine[ph], t0 = s.tfirst[ph];
+    const bool pairs = d.epi == EPI_QKV || d.epi == EPI_GU;
+    XBlock x;
+    if (lane_on) load_xblock(s, b, fh, x);
+    int buf = 0;
+    for (int k0 = 0; k0 < nm; k0 += TB) {
+        const int nt = min(TB, nm - k0);
+        // this thread's epilogue row of the batch, and its residual operand
+        const int eti = tid / R, er = tid - eti * R;
+        const int en = (t0 + (k0 + eti) * G) * R + er;
+        const bool e_on = tid < nt * R && en < N && (!pairs || (er & 1) == 0);
         float pre = 0.f;
-        if (d.epi == EPI_RESID && (lane & 3) == 0 && row < rows) pre = __ldcg(d.out + r0 + row);
-        // lane 0 waits for the tile's bytes; the warp sync orders the reads
-        int ok = 1;
-        if (lane == 0) {
-            const uint64_t t0 = tr.on ? globaltimer_ns() : 0;
-            ok = wait_mbar(p, &s.full[slot], (i / kStages) & 1u, ph, st.f) ? 1 : 0;
-            if (tr.on) tr.data_wait_ns += globaltimer_ns() - t0;
+        if (d.epi == EPI_RESID && e_on) pre = __ldcg(d.out + en);
+        float t[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = 0.f;
+        // 1. this warp's slices of the batch's tiles have landed (each thread
+        //    waits for its own copies, the warp sync publishes the others')
+        {
+            const uint64_t w0 = tr.on ? globaltimer_ns() : 0;
+            static_assert(TB <= kWarpSlots && TB <= 4, "batch waits below");
+            switch (nt) {
+                case 1: cp_async_wait<kWarpSlots - 1>(); break;
+                case 2: cp_async_wait<kWarpSlots - 2>(); break;
+                case 3: cp_async_wait<kWarpSlots - 3>(); break;
+                default: cp_async_wait<kWarpSlots - 4>(); break;
+            }
+            if (tr.on) tr.data_wait_ns += globaltimer_ns() - w0;
         }
-        ok = __shfl_sync(FULL, ok, 0);
-        if (!ok) return false;
-        const uint8_t* tq = s.ring[slot];
-        const uint16_t* ts = reinterpret_cast<const uint16_t*>(tq + static_cast<size_t>(rows) * K);
-        const float y = warp_tile<R>(tq, ts, s.u.xs, K, SK, rows);
         __syncwarp();
-        // the slot is free: refill it with the tile kStages ahead
-        if (lane == 0) {
-            Pos c{st.f, ph, k};
-            if (pos_advance(p, s, c, kStages)) issue_tile(s, c, i + kStages);
+        // 2. every unit of the batch: independent dot chains
+        if (lane_on) {
+#pragma unroll
+            for (int ti = 0; ti < TB; ++ti) {
+                if (ti < nt) {
+                    const uint32_t i = gidx + static_cast<uint32_t>(k0 + ti);
+                    const int r0 = (t0 + (k0 + ti) * G) * R;
+                    const int rows = min(R, N - r0);
+                    const uint8_t* ch = s.ring[warp][i % kWarpSlots];
+                    const uint16_t* cs = reinterpret_cast<const uint16_t*>(ch + M * nbw * 32);
+#pragma unroll
+                    for (int j = 0; j < M; ++j) {
+                        const int r = rl + RL * j;
+                        if (r < rows) t[ti * M + j] = unit_dot(ch + (j * nbw + lane) * 32, cs[j * nbwp + lane], x, fh);
+                    }
+                }
+            }
         }
-        epilogue(p, d, st, r0, rows, R, y, pre, pf.rc, pf.rs, best);
-        if (tr.on) tr.tiles += 1;
+        __syncwarp();  // the batch's slots are free
+        // 3. refill them, kWarpSlots tiles ahead
+        for (int ti = 0; ti < nt; ++ti)
+            stream_next(p, s, sw, gidx + static_cast<uint32_t>(k0 + ti + kWarpSlots), warp, lane);
+        if (tr.on) tr.tiles += static_cast<unsigned long long>(nt);
+        const float y8 = reduce8(t, lane);
+        if (warp_on && (lane & 3) == 0) s.part[buf][warp][lane >> 2] = y8;
+        // RoPE cos/sin of the epilogue pair (whole warps take part in the shuffles)
+        float c = 0.f, sn = 0.f;
+        if (d.epi == EPI_QKV) {
+            const int pair = (en % kHeadDim) >> 1;
+            c = __shfl_sync(FULL, pf.rc, pair & 31);
+            sn = __shfl_sync(FULL, pf.rs, pair & 31);
+        }
+        cbar();
+        if (e_on) {
+            const int erl = er % RL, v = eti * M + er / RL;
+            float y = 0.f, y1 = 0.f;
+            for (int w = 0; w < wpr; ++w) y += s.part[buf][erl * wpr + w][v];
+            if (pairs) {
+                const int erl1 = (er + 1) % RL, v1 = eti * M + (er + 1) / RL;
+                for (int w = 0; w < wpr; ++w) y1 += s.part[buf][erl1 * wpr + w][v1];
+            }
+            epilogue(p, d, st, en, y, y1, pre, c, sn, best);
+        }
+        buf ^= 1;
     }
     return true;
 }
 
 // One GEMV phase; returns false on timeout (this CTA then stops at the end
 // of the phase, together with its other warps).
-__device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
-                                           int ph, uint32_t gidx, const Prefetch& pf, TraceAcc& tr) {
+__device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, Stream& sw, const PhaseDesc& d,
+                                           const StepCtx& st, int ph, uint32_t gidx, const Prefetch& pf,
+                                           TraceAcc& tr) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nm = s.nmine[ph];
     if (nm == 0) {
@@ -634,12 +761,7 @@ __device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, const
     trace_mark(p, ph, st.f, 2);
     unsigned long long best = 0ull;
     bool ok;
-    switch (d.rows_per_tile) {
-        case 1: ok = gemv_tiles<1>(p, s, d, st, ph, gidx, pf, tr, best); break;
-        case 2: ok = gemv_tiles<2>(p, s, d, st, ph, gidx, pf, tr, best); break;
-        case 4: ok = gemv_tiles<4>(p, s, d, st, ph, gidx, pf, tr, best); break;
-        default: ok = gemv_tiles<8>(p, s, d, st, ph, gidx, pf, tr, best); break;
-    }
+    ok = gemv_tiles<kTileMult>(p, s, sw, d, st, ph, gidx, pf, tr, best);
     if (d.epi == EPI_LOGITS) {
 #pragma unroll
         for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(FULL, best, o));
@@ -818,7 +940,7 @@ __device__ __forceinline__ bool attn_prefetch(const DecodeParams& p, Smem& s, co
 // ---------------------------------------------------------------------------
 // the program loop
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void run(const DecodeParams& p, Smem& s) {
+__device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) {
     const int G = gridDim.x;
     const int tid = threadIdx.x;
     uint32_t gidx = 0;  // schedule index of the current phase's first tile
@@ -875,8 +997,8 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s) {
                         mbar_arrive(&s.abar);
                         wait_mbar(p, &s.abar, abar_phase & 1u, ph, f);
                     }
-                    drain_ring(p, s);
                 }
+                cp_async_wait_all();  // no weight copy may land after the CTA left
                 return;
             }
             trace_mark(p, ph, f, 1);
@@ -888,14 +1010,14 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s) {
                     st.token = s.token;
                     st.x0_given = (f == 0 && p.x0 != nullptr);
                 }
-                ok = gemv_phase(p, s, d, st, ph, gidx, pf, tr);
+                ok = gemv_phase(p, s, sw, d, st, ph, gidx, pf, tr);
                 gidx += static_cast<uint32_t>(s.nmine[ph]);
             }
             if (!ok) s.abort_flag = 1;  // any warp: the CTA stops after this phase
             // 2. release this phase once all warps wrote their outputs.
             cbar();
             if (s.abort_flag) {
-                if (tid == 0) drain_ring(p, s);
+                cp_async_wait_all();
                 return;
             }
             if (tid == 0) {
@@ -904,7 +1026,8 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s) {
                     for (int w = 0; w < kWarps; ++w) b = max(b, s.best[w]);
                     p.argmax_part[blockIdx.x] = b;
                 }
-                __threadfence();
+                // gpu-scope release of the phase: covers every store of the CTA
+                // ordered before it by the barrier above
                 red_release_gpu_add(p.counters + ph, 1u);
                 if (tr.on) {
                     unsigned long long* rec =
@@ -925,24 +1048,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x;
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&s.full[i], 1);
-            s.slot_issued[i] = 0;
-        }
         mbar_init(&s.abar, 1);
         s.abort_flag = 0;
         fence_mbar_init();
         build_schedule(p, s);
-        // fill the ring with the first kStages tiles of the schedule
-        Pos c{0, 0, 0};
-        bool more = s.nmine[0] > 0 || pos_advance(p, s, c, 0);
-        for (uint32_t i = 0; more && i < static_cast<uint32_t>(kStages); ++i) {
-            issue_tile(s, c, i);
-            more = pos_advance(p, s, c, 1);
-        }
     }
     __syncthreads();
-    run(p, s);
+    // every warp starts its weight stream: the first kWarpSlots tiles
+    const int warp = tid >> 5, lane = tid & 31;
+    Stream sw{Pos{0, 0, 0}, true, -1, nullptr, 0, 0};
+    sw.more = s.nmine[0] > 0 || pos_advance(p, s, sw.c, 0);
+    for (uint32_t i = 0; i < static_cast<uint32_t>(kWarpSlots); ++i) stream_next(p, s, sw, i, warp, lane);
+    run(p, s, sw);
+    cp_async_wait_all();
 }
 
 int decode_smem_bytes() { return static_cast<int>(sizeof(Smem)); }

@@ -69,6 +69,8 @@ const TensorInfo* gguf_find(const tir_gguf* g, const std::string& name);
 // ---- op-level kernel launchers (ops.cu) -------------------------------------
 int launch_repack(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* quants, uint16_t* scales,
                   int64_t sk, int64_t dst_row_step, int64_t dst_row_off, void* stream);
+int launch_repack_tiled(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* dst, int64_t n_total,
+                        int64_t tile_rows, int64_t dst_row_step, int64_t dst_row_off, void* stream);
 int launch_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, void* stream);
 int launch_rmsnorm(const float* x, const float* w, float* out, int64_t n, float eps, void* stream);
 int launch_softmax(const float* x, float* out, int64_t n, void* stream);
@@ -83,12 +85,13 @@ int launch_attention(const float* q, const float* kc, const float* vc, float* ou
 int launch_silu_mul(const float* gate, const float* up, float* out, int64_t n, void* stream);
 int launch_fill_f32(float* out, float v, int64_t n, void* stream);
 
-// Streaming Q8_0 matvec (decode.cu machinery, one phase).
+// Streaming Q8_0 matvec (decode.cu machinery, one phase) over the split
+// layout (quants, scales) or, with scales == NULL, the tile-major layout.
 tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out,
                             int64_t n, int64_t k, void* stream);
 
-// Tile rows of a [n][k] split-layout matrix in one ring stage.
-int tile_rows_for(int64_t k, int64_t n, int grid);
+// Rows per weight tile of a matrix with k columns (0: unsupported k).
+int tile_rows_for(int64_t k, bool pairs);
 
 // glibc-evaluated RoPE table for positions [0, max_ctx): cos/sin of
 // rope_angles (src/math.rs:181-193).

@@ -39,7 +39,7 @@ __device__ __forceinline__ int8_t f32_as_i8(float v) {
     return static_cast<int8_t>(v);
 }
 
-// Q8_0 blocks -> split layout (quants u = q + 128, f16 scales), optionally
+// Q8_0 blocks -> split layout (signed int8 quants, f16 scales), optionally
 // interleaving rows into the destination (dst row = r * step + off).
 __global__ void repack_kernel(const uint8_t* __restrict__ blocks, int64_t rows, int64_t k,
                               uint8_t* __restrict__ quants, uint16_t* __restrict__ scales, int64_t sk,
@@ -54,13 +54,42 @@ __global__ void repack_kernel(const uint8_t* __restrict__ blocks, int64_t rows, 
         uint32_t w[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-            w[j] = (static_cast<uint32_t>(src[2 + 4 * j]) | (static_cast<uint32_t>(src[3 + 4 * j]) << 8) |
-                    (static_cast<uint32_t>(src[4 + 4 * j]) << 16) | (static_cast<uint32_t>(src[5 + 4 * j]) << 24)) ^
-                   0x80808080u;
+            w[j] = static_cast<uint32_t>(src[2 + 4 * j]) | (static_cast<uint32_t>(src[3 + 4 * j]) << 8) |
+                   (static_cast<uint32_t>(src[4 + 4 * j]) << 16) | (static_cast<uint32_t>(src[5 + 4 * j]) << 24);
         uint4* dst = reinterpret_cast<uint4*>(quants + dr * k + b * 32);
         dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
         dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
         scales[dr * sk + b] = static_cast<uint16_t>(src[0] | (src[1] << 8));
+    }
+}
+
+// Q8_0 blocks -> warp-sliced tile-major layout (runtime.h q8_slice_offset):
+// row r of the source lands in row dr = r * step + off of the matrix.
+__global__ void repack_tiled_kernel(const uint8_t* __restrict__ blocks, int64_t rows, int64_t k,
+                                    uint8_t* __restrict__ dst, int64_t tile_rows, int64_t step, int64_t off) {
+    const int64_t nb = k / 32;
+    const int rl_n = gemv_row_lanes(k);
+    const int64_t total = rows * nb;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / nb, b = i % nb;
+        const uint8_t* src = blocks + i * 34;
+        const int64_t dr = r * step + off;
+        const int64_t t = dr / tile_rows, rr = dr % tile_rows;
+        const int rl = static_cast<int>(rr % rl_n), j = static_cast<int>(rr / rl_n);
+        const int wi = static_cast<int>(b / 32), bl = static_cast<int>(b % 32);
+        const int nbw = q8_slice_blocks(k, wi), nbwp = (nbw + 7) / 8 * 8;
+        uint8_t* base = dst + q8_slice_offset(k, t, rl, wi);
+        uint32_t w[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+            w[jj] = static_cast<uint32_t>(src[2 + 4 * jj]) | (static_cast<uint32_t>(src[3 + 4 * jj]) << 8) |
+                    (static_cast<uint32_t>(src[4 + 4 * jj]) << 16) | (static_cast<uint32_t>(src[5 + 4 * jj]) << 24);
+        uint4* q = reinterpret_cast<uint4*>(base + (static_cast<int64_t>(j) * nbw + bl) * 32);
+        q[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        q[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        reinterpret_cast<uint16_t*>(base + kTileMult * nbw * 32)[j * nbwp + bl] =
+            static_cast<uint16_t>(src[0] | (src[1] << 8));
     }
 }
 
@@ -209,7 +238,7 @@ __global__ void q8_act_matmul_kernel(const uint8_t* __restrict__ xb, const uint8
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const uint4 w = w4[h];
-                const uint32_t ws[4] = {w.x ^ 0x80808080u, w.y ^ 0x80808080u, w.z ^ 0x80808080u, w.w ^ 0x80808080u};
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int xv = x4[h * 4 + j];
@@ -325,6 +354,15 @@ int launch_repack(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* quant
     if (rows * (k / 32) == 0) return 0;
     repack_kernel<<<grid_for(rows * (k / 32), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         blocks, rows, k, quants, scales, sk, step, off);
+    return last_err();
+}
+
+int launch_repack_tiled(const uint8_t* blocks, int64_t rows, int64_t k, uint8_t* dst, int64_t n_total,
+                        int64_t tile_rows, int64_t step, int64_t off, void* stream) {
+    (void)n_total;
+    if (rows <= 0) return 0;
+    repack_tiled_kernel<<<grid_for(rows * (k / 32), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        blocks, rows, k, dst, tile_rows, step, off);
     return last_err();
 }
 

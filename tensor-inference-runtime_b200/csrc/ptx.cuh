@@ -1,5 +1,6 @@
 // ptx.cuh -- thin inline-PTX wrappers for sm_100a: mbarriers, the TMA bulk
-// (non-tensor) copy engine, gpu-scope acquire/release, named barriers.
+// (non-tensor) copy engine, cp.async, gpu-scope acquire/release, named
+// barriers.
 // No cluster multicast form is used anywhere in this runtime.
 #pragma once
 #include <cstdint>
@@ -80,6 +81,22 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
 __device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+
+// Asynchronous 16-byte copy global -> shared (L1 bypassed), tracked by the
+// issuing thread's commit groups.
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+// Waits until at most N of this thread's commit groups are still pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;

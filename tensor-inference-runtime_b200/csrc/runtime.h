@@ -20,16 +20,17 @@
 namespace tir {
 
 // ---- launch geometry --------------------------------------------------------
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;            // one CTA of 8 warps per SM
-constexpr int kStageBytes = 9216;                // one weight tile (ring slot)
-constexpr int kStages = 21;                      // ring depth
-constexpr int kMaxTileRows = 8;                  // rows per tile: 1, 2, 4 or 8
+constexpr int kWarps = 12;
+constexpr int kThreads = kWarps * 32;            // one CTA of 12 warps per SM
+constexpr int kTileMult = 2;                     // tile rows = row lanes x 2
+constexpr int kChunkBytes = kTileMult * 32 * 34; // one warp's slice of a tile: 2 rows x 32 blocks
+constexpr int kWarpSlots = 7;                    // per-warp ring depth (183 KB in flight per SM)
 constexpr int kMaxK = 6144;                      // longest matvec row (columns)
 constexpr int kMaxPhases = 128;                  // phases per step (5 per layer + 1)
 constexpr int kHeadDim = 64;                     // attention head size supported
 constexpr int kAttnChunk = 32;                   // positions per attention chunk
 constexpr int kAttnHeadsPerPass = kWarps;
+static_assert(kMaxK / 16 == kThreads, "input staging gives every thread one 16-column chunk");
 
 enum PhaseKind : int32_t { PH_GEMV = 0, PH_ATTN = 1 };
 // IN_ATTN: the attention output, merged from the per-split partial softmaxes
@@ -43,13 +44,49 @@ enum EpiKind : int32_t { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_GU = 3, 
 // Scale row stride (f16 elements) of the split Q8_0 layout: 16-byte rows.
 __host__ __device__ constexpr int64_t scale_stride(int64_t k) { return ((k / 32) + 7) / 8 * 8; }
 
+// GEMV geometry for rows of k columns (k / 32 Q8_0 blocks): a "row lane" of
+// gemv_wpr(k) warps covers one row, lane j of the group owning column block j;
+// the CTA's kWarps warps form gemv_row_lanes(k) row lanes, and a weight tile
+// holds row_lanes x kTileMult rows: row lane rl takes tile rows rl and
+// rl + row_lanes, so every thread handles kTileMult (row, block) units of
+// every tile with the same column block.
+__host__ __device__ constexpr int gemv_wpr(int64_t k) { return static_cast<int>((k / 32 + 31) / 32); }
+__host__ __device__ constexpr int gemv_row_lanes(int64_t k) { return kWarps / gemv_wpr(k); }
+__host__ __device__ constexpr int gemv_tile_rows(int64_t k) { return gemv_row_lanes(k) * kTileMult; }
+
+// Warp-sliced tile-major Q8_0 layout (the layout the decode kernel streams).
+// Tile t holds rows [t R, t R + R), R = gemv_tile_rows(k), the last tile
+// padded with zero rows.  Inside a tile, the slice of warp (row lane rl,
+// column warp wi) -- tile rows rl + row_lanes j (j < kTileMult), column
+// blocks [32 wi, 32 wi + nbw) -- is one contiguous chunk: the rows' quants
+// (kTileMult x nbw x 32 int8), then their f16 scales (kTileMult x nbwp,
+// nbwp = nbw rounded up to 8).  Chunks follow in (rl, wi) order, so each
+// warp streams its own slice of every tile with 16-byte copies.
+__host__ __device__ constexpr int q8_slice_blocks(int64_t k, int wi) {
+    return static_cast<int>((k / 32 - 32 * wi) < 32 ? (k / 32 - 32 * wi) : 32);
+}
+__host__ __device__ constexpr int64_t q8_slice_bytes(int64_t k, int wi) {
+    return kTileMult * (q8_slice_blocks(k, wi) * 32 + ((q8_slice_blocks(k, wi) + 7) / 8 * 8) * 2);
+}
+__host__ __device__ constexpr int64_t q8_lane_bytes(int64_t k) {
+    return (gemv_wpr(k) - 1) * q8_slice_bytes(k, 0) + q8_slice_bytes(k, gemv_wpr(k) - 1);
+}
+__host__ __device__ constexpr int64_t q8_tile_bytes(int64_t k) { return gemv_row_lanes(k) * q8_lane_bytes(k); }
+__host__ __device__ constexpr int64_t q8_slice_offset(int64_t k, int64_t t, int rl, int wi) {
+    return t * q8_tile_bytes(k) + rl * q8_lane_bytes(k) + wi * q8_slice_bytes(k, 0);
+}
+__host__ __device__ constexpr int64_t q8_tiled_matrix_bytes(int64_t n, int64_t k) {
+    return (n + gemv_tile_rows(k) - 1) / gemv_tile_rows(k) * q8_tile_bytes(k);
+}
+
 struct PhaseDesc {
     int32_t kind, layer, in_kind, epi;
     int32_t n, k, sk;          // rows, columns, scale stride (halves)
-    int32_t rows_per_tile, n_tiles;
+    int32_t rows_per_tile, n_tiles;  // rows_per_tile = gemv_tile_rows(k)
     int32_t dump;              // EPI_RESID: also write the residual to the dump
-    const uint8_t* wq;         // quants [n][k], q + 128
-    const uint16_t* ws;        // f16 scales [n][sk]
+    int32_t tiled;             // 1: wq is warp-sliced tile-major (q8_slice_offset), ws unused
+    const uint8_t* wq;         // quants [n][k] signed int8 q (split layout), or the tiled matrix
+    const uint16_t* ws;        // f16 scales [n][sk] (split layout)
     const float* in;           // IN_RAW input / IN_X_NORM residual buffer
     const float* norm_w;       // rmsnorm weights (IN_*_NORM)
     float* out;                // epilogue target

@@ -74,7 +74,7 @@ tir_status matvec(const float* x, const uint8_t* quants, const uint16_t* scales,
     d.n = static_cast<int32_t>(n);
     d.k = static_cast<int32_t>(k);
     d.sk = static_cast<int32_t>(scale_stride(k));
-    d.rows_per_tile = tile_rows_for(k, n, sms);
+    d.rows_per_tile = tile_rows_for(k, false);
     d.n_tiles = static_cast<int32_t>((n + d.rows_per_tile - 1) / d.rows_per_tile);
     d.wq = quants;
     d.ws = scales;

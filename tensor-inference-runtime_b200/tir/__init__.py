@@ -115,6 +115,10 @@ SIGNATURES = {
     "tir_rope_angles": (None, [C.c_float, _i64, _i64, _f32p]),
     "tir_swiglu": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_swiglu_static": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "tir_q8_tile_rows": (_i64, [_i64]),
+    "tir_q8_tiled_bytes": (_i64, [_i64, _i64]),
+    "tir_q8_repack_tiled": (C.c_int, [_vp, _i64, _i64, _vp, _vp]),
+    "tir_q8_matmul_tiled": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_activated_q8": (C.c_int, [_vp, _i64, _vp, _vp]),
     "tir_q8_act_matmul": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_argmax": (C.c_int, [_vp, _i64, _vp, _vp]),
@@ -424,6 +428,22 @@ def q8_repack(blocks, rows, k, quants, scales, stream=None):
 
 def q8_matmul(x, quants, scales, out, n, k, stream=None):
     check(lib().tir_q8_matmul(_ptr(x), _ptr(quants), _ptr(scales), _ptr(out), n, k, _stream(stream)))
+
+
+def q8_tile_rows(k):
+    return lib().tir_q8_tile_rows(k)
+
+
+def q8_tiled_bytes(n, k):
+    return lib().tir_q8_tiled_bytes(n, k)
+
+
+def q8_repack_tiled(blocks, rows, k, out, stream=None):
+    check(lib().tir_q8_repack_tiled(_ptr(blocks), rows, k, _ptr(out), _stream(stream)))
+
+
+def q8_matmul_tiled(x, w, out, n, k, stream=None):
+    check(lib().tir_q8_matmul_tiled(_ptr(x), _ptr(w), _ptr(out), n, k, _stream(stream)))
 
 
 def q8_dequant(blocks, n_blocks, out, stream=None):

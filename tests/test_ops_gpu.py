@@ -39,7 +39,7 @@ def test_repack_layout(cuda, tirlib):
     x, blocks = synth.gemv_case(1408, 6, seed=2)
     q, s = split_layout(torch, tirlib, blocks, 6, 1408)
     b = blocks.reshape(6, 44, 34)
-    np.testing.assert_array_equal(host(q).reshape(6, 1408), (b[:, :, 2:].reshape(6, 1408) ^ 0x80))
+    np.testing.assert_array_equal(host(q).reshape(6, 1408), b[:, :, 2:].reshape(6, 1408))
     sk = tirlib.q8_scale_stride(1408)
     sc = host(s).view(np.uint16).reshape(6, sk)
     np.testing.assert_array_equal(sc[:, :44], b[:, :, :2].copy().view(np.uint16).reshape(6, 44))
@@ -61,6 +61,65 @@ def test_q8_matmul_vs_oracle(cuda, tirlib, orc, k, n):
     tirlib.q8_matmul(dev(torch, x), q, s, out, n, k)
     got = host(out)
     # f32 with a different summation order: rel-L2 bound 1e-5 (observed ~1e-7)
+    assert rel_l2(got, ref) < 1e-5
+    scale = np.abs(x).sum() * 127 * np.abs(blocks.reshape(n, -1, 34)[:, :, :2].copy().view(np.float16)).max()
+    assert np.max(np.abs(got - ref)) < 1e-5 * scale + 1e-30
+
+
+def tiled_layout(torch, tirlib, blocks, rows, k):
+    w = torch.empty(tirlib.q8_tiled_bytes(rows, k), dtype=torch.uint8, device="cuda")
+    tirlib.q8_repack_tiled(dev(torch, np.ascontiguousarray(blocks, np.uint8).reshape(-1)), rows, k, w)
+    return w
+
+
+def test_repack_tiled_layout(cuda, tirlib):
+    """Warp-sliced tile-major layout: tiles of R rows (last one zero-padded);
+    in a tile, the slice of (row lane rl, column warp wi) -- rows rl + RL j
+    (j < 2), blocks [32 wi, 32 wi + nbw) -- is one chunk: quants, then f16
+    scales (nbw rounded up to 8 per row), chunks in (rl, wi) order."""
+    torch = cuda
+    for rows, k in [(29, 1408), (5, 5632), (7, 96)]:
+        _, blocks = synth.gemv_case(k, rows, seed=5)
+        w = host(tiled_layout(torch, tirlib, blocks, rows, k))
+        nb = k // 32
+        wpr = (nb + 31) // 32
+        RL = 12 // wpr
+        R = tirlib.q8_tile_rows(k)
+        assert R == 2 * RL
+        nbws = [min(32, nb - 32 * wi) for wi in range(wpr)]
+        slice_bytes = [2 * (b * 32 + (b + 7) // 8 * 8 * 2) for b in nbws]
+        lane_bytes = sum(slice_bytes)
+        tile_bytes = RL * lane_bytes
+        n_tiles = -(-rows // R)
+        assert w.size == n_tiles * tile_bytes
+        b = blocks.reshape(rows, nb, 34)
+        seen = np.zeros(w.size, bool)
+        for r in range(rows):
+            t, rr = divmod(r, R)
+            j, rl = divmod(rr, RL)
+            for blk in range(nb):
+                wi, bl = divmod(blk, 32)
+                nbw = nbws[wi]
+                base = t * tile_bytes + rl * lane_bytes + sum(slice_bytes[:wi])
+                q = base + (j * nbw + bl) * 32
+                sc = base + 2 * nbw * 32 + (j * ((nbw + 7) // 8 * 8) + bl) * 2
+                np.testing.assert_array_equal(w[q:q + 32], b[r, blk, 2:])
+                np.testing.assert_array_equal(w[sc:sc + 2], b[r, blk, :2])
+                seen[q:q + 32] = True
+                seen[sc:sc + 2] = True
+        assert np.all(w[~seen] == 0)  # scale padding and padded rows
+
+
+@pytest.mark.parametrize("k,n", [(2048, 2048), (2048, 256), (5632, 2048), (2048, 32000), (1408, 100), (96, 7),
+                                 (6144, 40), (512, 1)])
+def test_q8_matmul_tiled_vs_oracle(cuda, tirlib, orc, k, n):
+    torch = cuda
+    x, blocks = synth.gemv_case(k, n, seed=k + n)
+    ref = orc.q8_matmul(x, blocks.reshape(-1), n)
+    w = tiled_layout(torch, tirlib, blocks, n, k)
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    tirlib.q8_matmul_tiled(dev(torch, x), w, out, n, k)
+    got = host(out)
     assert rel_l2(got, ref) < 1e-5
     scale = np.abs(x).sum() * 127 * np.abs(blocks.reshape(n, -1, 34)[:, :, :2].copy().view(np.float16)).max()
     assert np.max(np.abs(got - ref)) < 1e-5 * scale + 1e-30
