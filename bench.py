@@ -37,6 +37,14 @@ WORKLOAD = ("TinyLlama-1.1B-shape Llama-2 decoder (22 layers, hidden 2048, 32/4 
 METRIC = "decode tok/s (batch 1)"
 
 
+def workload_name(args):
+    if args.prompt == 16 and args.decode == 128:
+        return WORKLOAD
+    return WORKLOAD.replace("16-token seeded prompt + 128 steps (144 forwards per step)",
+                            f"{args.prompt}-token seeded prompt + {args.decode} steps "
+                            f"({args.prompt + args.decode} forwards per step)")
+
+
 def parse_args(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -47,13 +55,17 @@ def parse_args(argv=None):
     ap.add_argument("--decode", type=int, default=128)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--cpu-baseline", choices=["auto", "off"], default="auto")
-    ap.add_argument("--workload", choices=["decode", "gemv"], default="decode",
-                    help="decode: the batch-1 decode loop (default); gemv: the isolated Q8_0 GEMV sweep "
-                         "over the TinyLlama projection shapes")
+    ap.add_argument("--workload", choices=["decode", "long", "gemv"], default="decode",
+                    help="decode: the batch-1 decode loop, 16 prompt ids + 128 steps (default); long: the same "
+                         "loop with a 1792-id prompt + 256 steps (context 2048); gemv: the isolated Q8_0 GEMV "
+                         "sweep over the TinyLlama projection shapes")
     ap.add_argument("--timeline", metavar="FILE.md", default=None,
                     help="after the timed region, trace forward step 100 of one more generate "
                          "and write the per-phase timeline summary to FILE.md")
-    return ap.parse_args(argv)
+    args = ap.parse_args(argv)
+    if args.workload == "long":
+        args.prompt, args.decode = 1792, 256
+    return args
 
 
 # ---------------------------------------------------------------------------
@@ -187,7 +199,7 @@ def run_reference(args, dist):
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0 weights and token ids)",
-            "config": {"workload": WORKLOAD, "batch": 1, "prompt_tokens": args.prompt,
+            "config": {"workload": workload_name(args), "batch": 1, "prompt_tokens": args.prompt,
                        "decode_tokens": args.decode, "parallelism": "host cores"},
             "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": orc.get_threads(), "kind": "port",
@@ -293,7 +305,8 @@ def run_ours(args, dist):
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0 weights and token ids)",
-        "config": {"workload": WORKLOAD, "batch": 1, "prompt_tokens": args.prompt, "decode_tokens": args.decode,
+        "config": {"workload": workload_name(args), "batch": 1, "prompt_tokens": args.prompt,
+                   "decode_tokens": args.decode,
                    "forwards_per_step": n_fwd, "parallelism": f"replicas x{dist.world} (no collective)",
                    "l2": "inputs larger than L2: 1.10 GB of weights streamed per forward vs 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
