@@ -229,6 +229,19 @@ tir_status tir_q8_repack_tiled(const uint8_t *blocks, int64_t rows, int64_t k, u
 /* q8_matmul (src/math.rs:87-98) over the tile-major layout. */
 tir_status tir_q8_matmul_tiled(const float *x, const uint8_t *w, float *out, int64_t n, int64_t k,
                                void *stream);
+/* Batched q8_matmul: the reference's q8_matmul (src/math.rs:87-98) applied to
+ * many tokens at once (its forward, src/forward.rs:261-275, does it token by
+ * token), on the sm_100a tensor cores.  The weights first go into the
+ * tensor-core layout: tir_q8_gemm_bytes(n, k) bytes plus tir_q8_gemm_rows(n)
+ * floats (a power of two per row), prepared once from Q8_0 blocks on the
+ * device.  Then y[t][j] = sum_c x[t][c] * W[j][c] (f32, y row stride n) for
+ * t < tokens; k must be a multiple of 64. */
+int64_t tir_q8_gemm_bytes(int64_t n, int64_t k);
+int64_t tir_q8_gemm_rows(int64_t n);
+tir_status tir_q8_gemm_prepare(const uint8_t *blocks, int64_t n, int64_t k, uint8_t *w, float *w_pow2,
+                               void *stream);
+tir_status tir_q8_matmul_batch(const float *x, int64_t tokens, const uint8_t *w, const float *w_pow2,
+                               float *y, int64_t n, int64_t k, void *stream);
 /* q8_matmul (src/math.rs:87-98): out[n] = sum_b f32(s[n,b]) * sum_i x[32b+i]*q[n,b,i].
  * Streaming sm_100a GEMV over the split layout. */
 tir_status tir_q8_matmul(const float *x, const uint8_t *quants, const uint16_t *scales,

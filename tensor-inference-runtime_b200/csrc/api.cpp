@@ -9,6 +9,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -1020,6 +1021,54 @@ tir_status tir_q8_matmul_tiled(const float* x, const uint8_t* w, float* out, int
     if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
     if (!w) return fail(TIR_ERR_INVALID_ARG, "null weights");
     return q8_matmul_stream(x, w, nullptr, out, n, k, stream);
+}
+
+int64_t tir_q8_gemm_bytes(int64_t n, int64_t k) {
+    if (n <= 0 || k <= 0 || k % 64 != 0) return -1;
+    return gemm_q8_weight_bytes(n, k);
+}
+
+int64_t tir_q8_gemm_rows(int64_t n) { return n <= 0 ? 0 : gemm_q8_rows_padded(n); }
+
+tir_status tir_q8_gemm_prepare(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* w, float* w_pow2, void* stream) {
+    clear_error();
+    if (n <= 0 || k <= 0 || k % 64 != 0)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "tensor-core layout needs n > 0 and k a positive multiple of 64");
+    if (!blocks || !w || !w_pow2) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    return op_rc(launch_gemm_repack(blocks, n, k, w, w_pow2, stream), "gemm repack");
+}
+
+tir_status tir_q8_matmul_batch(const float* x, int64_t tokens, const uint8_t* w, const float* w_pow2, float* y,
+                               int64_t n, int64_t k, void* stream) {
+    clear_error();
+    if (tokens < 0 || n <= 0 || k <= 0 || k % 64 != 0 || n > INT32_MAX / 2 || tokens > INT32_MAX / 2)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "batched q8 matmul needs n > 0 and k a positive multiple of 64");
+    if (!x || !w || !w_pow2 || !y) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (tokens == 0) return TIR_OK;
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    DevCtx* c = dev_ctx(dev);
+    if (!c) return fail(TIR_ERR_OOM, "device context allocation failed");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int sms = decode_grid_size(dev);
+    const int64_t tiles = ((n + 127) / 128) * ((tokens + 127) / 128);
+    int splits = 1;
+    if (tiles < sms) splits = static_cast<int>(std::min<int64_t>(k / 64, std::max<int64_t>(1, sms / tiles)));
+    uint8_t* planes = nullptr;
+    float* inv = nullptr;
+    float* part = nullptr;
+    const size_t pbytes = static_cast<size_t>(gemm_x_plane_bytes(tokens, k));
+    const size_t ibytes = static_cast<size_t>(gemm_tokens_padded(tokens)) * 4;
+    const size_t sbytes = splits > 1 ? static_cast<size_t>(splits) * tokens * n * 4 : 0;
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&planes), pbytes + ibytes + sbytes, st), "batched matmul scratch");
+    inv = reinterpret_cast<float*>(planes + pbytes);
+    part = splits > 1 ? reinterpret_cast<float*>(planes + pbytes + ibytes) : nullptr;
+    int rc = launch_gemm_x_planes(x, tokens, k, planes, inv, stream);
+    if (rc == 0)
+        rc = launch_gemm_q8(w, w_pow2, planes, inv, n, k, tokens, y, n, splits, part, c->error, timeout_ns(), stream);
+    cudaFreeAsync(planes, st);
+    if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "batched q8 matmul");
+    return TIR_OK;
 }
 
 tir_status tir_q8_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, void* stream) {

@@ -90,6 +90,17 @@ int launch_fill_f32(float* out, float v, int64_t n, void* stream);
 tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out,
                             int64_t n, int64_t k, void* stream);
 
+// Batched Q8_0 matmul on the tensor cores (gemm.cu).
+int64_t gemm_q8_weight_bytes(int64_t n, int64_t k);
+int64_t gemm_q8_rows_padded(int64_t n);
+int64_t gemm_x_plane_bytes(int64_t tokens, int64_t k);
+int64_t gemm_tokens_padded(int64_t tokens);
+int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out, float* pow2, void* stream);
+int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream);
+int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes, const float* x_inv, int64_t n,
+                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int splits, float* part, uint32_t* err,
+                   unsigned long long timeout_ns, void* stream);
+
 // Rows per weight tile of a matrix with k columns (0: unsupported k).
 int tile_rows_for(int64_t k, bool pairs);
 

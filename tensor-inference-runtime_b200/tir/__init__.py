@@ -115,6 +115,10 @@ SIGNATURES = {
     "tir_rope_angles": (None, [C.c_float, _i64, _i64, _f32p]),
     "tir_swiglu": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_swiglu_static": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "tir_q8_gemm_bytes": (_i64, [_i64, _i64]),
+    "tir_q8_gemm_rows": (_i64, [_i64]),
+    "tir_q8_gemm_prepare": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "tir_q8_matmul_batch": (C.c_int, [_vp, _i64, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_q8_tile_rows": (_i64, [_i64]),
     "tir_q8_tiled_bytes": (_i64, [_i64, _i64]),
     "tir_q8_repack_tiled": (C.c_int, [_vp, _i64, _i64, _vp, _vp]),
@@ -428,6 +432,20 @@ def q8_repack(blocks, rows, k, quants, scales, stream=None):
 
 def q8_matmul(x, quants, scales, out, n, k, stream=None):
     check(lib().tir_q8_matmul(_ptr(x), _ptr(quants), _ptr(scales), _ptr(out), n, k, _stream(stream)))
+
+
+def q8_gemm_prepare(blocks, n, k, stream=None):
+    """Tensor-core layout of a Q8_0 [n][k] matrix from device blocks: (w, w_pow2)."""
+    import torch
+    w = torch.empty(lib().tir_q8_gemm_bytes(n, k), dtype=torch.uint8, device=blocks.device)
+    p2 = torch.empty(lib().tir_q8_gemm_rows(n), dtype=torch.float32, device=blocks.device)
+    check(lib().tir_q8_gemm_prepare(_ptr(blocks), n, k, _ptr(w), _ptr(p2), _stream(stream)))
+    return w, p2
+
+
+def q8_matmul_batch(x, tokens, w, y, n, k, stream=None):
+    """y[t][j] = sum_c x[t][c] W[j][c] on the tensor cores; w = (weights, pow2)."""
+    check(lib().tir_q8_matmul_batch(_ptr(x), tokens, _ptr(w[0]), _ptr(w[1]), _ptr(y), n, k, _stream(stream)))
 
 
 def q8_tile_rows(k):
