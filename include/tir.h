@@ -210,6 +210,28 @@ tir_status tir_state_enable_trace(tir_state *s, int32_t step);
 tir_status tir_state_trace_dims(const tir_state *s, int32_t *n_phases, int32_t *grid);
 tir_status tir_state_trace(tir_state *s, uint64_t *out_host);
 
+/* ---- batched sequences: many tokens per forward --------------------------- */
+/* n_seqs independent sequences advancing in lockstep (batched greedy decode and
+ * batched prefill); each sequence computes what generate_capped
+ * (src/lib.rs:239-314) computes for it alone, with every projection on the
+ * tensor cores (tir_q8_matmul_batch).  The batch keeps its own KV caches
+ * (n_seqs x max_ctx positions) and a tensor-core copy of the model's weights. */
+typedef struct tir_batch tir_batch;
+tir_status tir_batch_create(tir_model *m, int32_t n_seqs, int32_t max_ctx, int32_t max_tokens_per_seq,
+                            tir_batch **out);
+void tir_batch_destroy(tir_batch *b);
+tir_status tir_batch_reset(tir_batch *b);
+int32_t tir_batch_len(const tir_batch *b);
+void *tir_batch_stream(tir_batch *b);
+/* Appends tokens_per_seq ids to every sequence (ids_host [n_seqs][tokens_per_seq])
+ * and returns each sequence's greedy next id (next_ids_host [n_seqs], may be NULL). */
+tir_status tir_batch_step(tir_batch *b, const int32_t *ids_host, int32_t tokens_per_seq,
+                          int32_t *next_ids_host);
+/* Per sequence: prompt (prompts_host [n_seqs][n_prompt]) then cap greedy steps,
+ * n_prompt + cap forwards as generate_capped; out_ids_host [n_seqs][cap]. */
+tir_status tir_batch_generate(tir_batch *b, const int32_t *prompts_host, int32_t n_prompt, int32_t cap,
+                              int32_t *out_ids_host);
+
 /* ---- op-level kernels (device pointers, asynchronous on `stream`) --------- */
 
 /* Q8_0 blocks (34 B: f16 scale LE + 32 int8) of a [rows][k] tensor into the

@@ -146,33 +146,12 @@ using namespace tir;
 // ---------------------------------------------------------------------------
 // model / state objects
 // ---------------------------------------------------------------------------
-// A weight matrix in HBM: tile-major (q = the tiled matrix, s unused, r rows
-// per tile) for the streamed projections, split (q [n][k], s [n][sk]) for the
-// embedding table, which is read one row at a time.
-struct Mat {
-    uint8_t* q = nullptr;
-    uint16_t* s = nullptr;
-    int64_t n = 0, k = 0, sk = 0, r = 0;
-    bool tiled = false;
-};
-
-struct tir_model {
-    int device = 0;
-    tir_transformer t{};
-    uint8_t* dev = nullptr;
-    size_t dev_bytes = 0;
-    uint64_t weight_bytes = 0;  // quants + scales + norm weights
-    std::vector<Mat> qkv, o, gu, down;
-    Mat lm, embd;
-    std::vector<float*> attn_norm, ffn_norm;
-    float* out_norm = nullptr;
-    ~tir_model() {
-        if (dev) {
-            cudaSetDevice(device);
-            cudaFree(dev);
-        }
+tir_model::~tir_model() {
+    if (dev) {
+        cudaSetDevice(device);
+        cudaFree(dev);
     }
-};
+}
 
 struct tir_state {
     tir_model* m = nullptr;

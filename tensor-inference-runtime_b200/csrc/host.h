@@ -58,6 +58,33 @@ struct tir_gguf {
 };
 
 namespace tir {
+// A weight matrix in HBM: tile-major (q = the tiled matrix, s unused, r rows
+// per tile) for the streamed projections, split (q [n][k], s [n][sk]) for the
+// embedding table, which is read one row at a time.
+struct Mat {
+    uint8_t* q = nullptr;
+    uint16_t* s = nullptr;
+    int64_t n = 0, k = 0, sk = 0, r = 0;
+    bool tiled = false;
+};
+
+}  // namespace tir
+
+struct tir_model {
+    int device = 0;
+    tir_transformer t{};
+    uint8_t* dev = nullptr;
+    size_t dev_bytes = 0;
+    uint64_t weight_bytes = 0;  // quants + scales + norm weights
+    std::vector<tir::Mat> qkv, o, gu, down;
+    tir::Mat lm, embd;
+    std::vector<float*> attn_norm, ffn_norm;
+    float* out_norm = nullptr;
+    ~tir_model();
+};
+
+namespace tir {
+
 // Parses a complete file image held by `g` (g->data/len set): load_model's
 // parse (src/lib.rs:29-138).
 tir_status gguf_parse_all(tir_gguf* g);

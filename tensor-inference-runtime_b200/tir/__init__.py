@@ -115,6 +115,13 @@ SIGNATURES = {
     "tir_rope_angles": (None, [C.c_float, _i64, _i64, _f32p]),
     "tir_swiglu": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_swiglu_static": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "tir_batch_create": (C.c_int, [_vp, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_vp)]),
+    "tir_batch_destroy": (None, [_vp]),
+    "tir_batch_reset": (C.c_int, [_vp]),
+    "tir_batch_len": (C.c_int32, [_vp]),
+    "tir_batch_stream": (_vp, [_vp]),
+    "tir_batch_step": (C.c_int, [_vp, _vp, C.c_int32, _vp]),
+    "tir_batch_generate": (C.c_int, [_vp, _vp, C.c_int32, C.c_int32, _vp]),
     "tir_q8_gemm_bytes": (_i64, [_i64, _i64]),
     "tir_q8_gemm_rows": (_i64, [_i64]),
     "tir_q8_gemm_prepare": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
@@ -432,6 +439,52 @@ def q8_repack(blocks, rows, k, quants, scales, stream=None):
 
 def q8_matmul(x, quants, scales, out, n, k, stream=None):
     check(lib().tir_q8_matmul(_ptr(x), _ptr(quants), _ptr(scales), _ptr(out), n, k, _stream(stream)))
+
+
+class Batch:
+    """n_seqs sequences decoded in lockstep on the tensor-core path."""
+
+    def __init__(self, model, n_seqs, max_ctx, max_tokens_per_seq):
+        self.model = model
+        self.n_seqs = n_seqs
+        h = C.c_void_p()
+        check(lib().tir_batch_create(model.handle, n_seqs, max_ctx, max_tokens_per_seq, C.byref(h)))
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().tir_batch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def reset(self):
+        check(lib().tir_batch_reset(self._h))
+
+    def __len__(self):
+        return lib().tir_batch_len(self._h)
+
+    def stream(self):
+        return lib().tir_batch_stream(self._h)
+
+    def step(self, ids):
+        """ids [n_seqs][tokens_per_seq] -> greedy next id per sequence."""
+        ids = np.ascontiguousarray(ids, np.int32).reshape(self.n_seqs, -1)
+        out = np.zeros(self.n_seqs, np.int32)
+        check(lib().tir_batch_step(self._h, ids.ctypes.data, ids.shape[1], out.ctypes.data))
+        return out
+
+    def generate(self, prompts, cap):
+        """prompts [n_seqs][n_prompt] -> ids [n_seqs][cap] (n_prompt + cap forwards each)."""
+        prompts = np.ascontiguousarray(prompts, np.int32).reshape(self.n_seqs, -1)
+        out = np.zeros((self.n_seqs, cap), np.int32)
+        check(lib().tir_batch_generate(self._h, prompts.ctypes.data, prompts.shape[1], cap, out.ctypes.data))
+        return out
 
 
 def q8_gemm_prepare(blocks, n, k, stream=None):
