@@ -12,10 +12,11 @@
 // accumulate in TMEM; the dropped a_lo x_lo term is below 2^-21 of the
 // product, and the powers of two are divided out exactly in the epilogue.
 //
-// Data flow per CTA (one 128-row weight tile x one 128-token tile, K in steps
-// of 64): warp 0 streams each step's raw Q8_0 block (8.5 KB) and the step's
-// pre-split activation planes (32 KB) with TMA bulk copies into a 3-stage
-// ring; warps 2-5 expand the raw block into the 128B-swizzled f16 hi/lo A
+// Data flow per CTA (one 128-row weight tile x one NT-token tile, NT = 256,
+// or 64 for small batches; K in steps of 64): warp 0 streams each step's raw
+// Q8_0 block (8.5 KB) and the step's pre-split activation planes (NT x 256 B)
+// with TMA bulk copies into a 2- or 3-stage ring (each SM's copy engine spends
+// a fixed time per copy, so the copies are few and large); warps 2-5 expand the raw block into the 128B-swizzled f16 hi/lo A
 // planes; one thread of warp 1 issues the 12 tcgen05.mma of the step (4 K
 // sub-steps x 3 passes) and commits the stage back to the producer; after the
 // last step warps 2-5 read the f32 accumulator out of TMEM.
@@ -35,27 +36,32 @@ namespace {
 
 constexpr int kGM = 128;    // weight rows per tile (UMMA M)
 constexpr int kGKS = 64;    // K per stage: one 128-byte f16 row
-constexpr int kGNT = 128;   // tokens per tile (UMMA N)
-constexpr int kGStages = 3;
 constexpr int kGThreads = 192;
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
-constexpr int kGPlane = kGNT * kGKS * 2;            // one f16 plane of a stage (16 KB)
+constexpr int kGPlaneA = kGM * kGKS * 2;            // one f16 weight plane of a stage (16 KB)
 constexpr uint32_t kGErrTimeout = 25;
 
-static_assert(kGNT == kGM, "A and X planes share the plane size");
+template <int NT>
+struct GemmCfg {
+    static constexpr int kStages = NT >= 256 ? 2 : 3;
+    static constexpr int kPlaneX = NT * kGKS * 2;  // one f16 activation plane of a stage
+};
 
+template <int NT>
 struct GemmSmem {
-    uint8_t a[kGStages][2 * kGPlane];  // weight planes hi | lo (128B-swizzled, K-major)
-    uint8_t x[kGStages][2 * kGPlane];  // activation planes hi | lo, copied as laid out in global
-    uint8_t w[kGStages][kGWBytes];     // raw Q8_0 block of the step (TMA target)
-    uint64_t full_raw[kGStages], full_a[kGStages], empty[kGStages], acc;
+    static constexpr int S = GemmCfg<NT>::kStages;
+    uint8_t a[S][2 * kGPlaneA];                   // weight planes hi | lo (128B-swizzled, K-major)
+    uint8_t x[S][2 * GemmCfg<NT>::kPlaneX];       // activation planes hi | lo, as laid out in global
+    uint8_t w[S][kGWBytes];                       // raw Q8_0 block of the step (TMA target)
+    uint64_t full_raw[S], full_a[S], empty[S], acc;
     uint32_t tmem_base;
     int32_t ok;
-    float inv_x[kGNT];
+    float inv_x[NT];
 };
-static_assert(offsetof(GemmSmem, x) % 1024 == 0 && offsetof(GemmSmem, w) % 16 == 0, "swizzle atoms need 1 KB");
-static_assert(offsetof(GemmSmem, full_raw) % 8 == 0, "mbarrier alignment");
-constexpr size_t kGSmemBytes = sizeof(GemmSmem) + 1024;  // + alignment slack
+static_assert(offsetof(GemmSmem<256>, x) % 1024 == 0 && offsetof(GemmSmem<64>, x) % 1024 == 0,
+              "swizzle atoms need 1 KB");
+static_assert(sizeof(GemmSmem<256>) + 1024 <= 227 * 1024 && sizeof(GemmSmem<64>) + 1024 <= 227 * 1024,
+              "shared memory budget");
 
 struct GemmParams {
     const uint8_t* w;        // tiled weights: [row tile][k step] blocks of kGWBytes
@@ -123,9 +129,13 @@ __device__ __forceinline__ bool gwait(const GemmParams& p, uint64_t* bar, uint32
     }
 }
 
+template <int NT>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_constant__ GemmParams p) {
+    constexpr int kGStages = GemmCfg<NT>::kStages;
+    constexpr int kGPlaneX = GemmCfg<NT>::kPlaneX;
     extern __shared__ uint8_t g_smem_raw[];
-    GemmSmem& s = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~uintptr_t(1023));
+    GemmSmem<NT>& s =
+        *reinterpret_cast<GemmSmem<NT>*>((reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rt = blockIdx.x, tt = blockIdx.y, split = blockIdx.z;
     const int nks_all = p.k / kGKS;
@@ -143,10 +153,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
-                     "r"(static_cast<uint32_t>(kGNT)));
+                     "r"(static_cast<uint32_t>(NT)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    for (int i = tid; i < kGNT; i += kGThreads) s.inv_x[i] = p.x_inv[tt * kGNT + i];
+    for (int i = tid; i < NT; i += kGThreads) s.inv_x[i] = p.x_inv[tt * NT + i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -161,10 +171,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                     s.ok = 0;
                     break;
                 }
-                mbar_arrive_expect_tx(&s.full_raw[st], kGWBytes + 2 * kGPlane);
+                mbar_arrive_expect_tx(&s.full_raw[st], kGWBytes + 2 * kGPlaneX);
                 bulk_g2s(s.w[st], p.w + (static_cast<size_t>(rt) * nks_all + ks0 + i) * kGWBytes, kGWBytes,
                          &s.full_raw[st]);
-                bulk_g2s(s.x[st], p.xp + (static_cast<size_t>(tt) * nks_all + ks0 + i) * (2 * kGPlane), 2 * kGPlane,
+                bulk_g2s(s.x[st], p.xp + (static_cast<size_t>(tt) * nks_all + ks0 + i) * (2 * kGPlaneX), 2 * kGPlaneX,
                          &s.full_raw[st]);
             }
             // every copy issued lands before the CTA can leave
@@ -173,7 +183,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     } else if (warp == 1) {
         // ---- MMA issue (one thread)
         if (lane == 0) {
-            const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(kGNT >> 3) << 17) | (static_cast<uint32_t>(kGM >> 4) << 24);
+            const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>(kGM >> 4) << 24);
             for (int i = 0; i < nks; ++i) {
                 const int st = i % kGStages;
                 if (!gwait(p, &s.full_raw[st], (i / kGStages) & 1) || !gwait(p, &s.full_a[st], (i / kGStages) & 1)) {
@@ -181,8 +191,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_hi = smem_u32(s.a[st]), a_lo = a_hi + kGPlane;
-                const uint32_t x_hi = smem_u32(s.x[st]), x_lo = x_hi + kGPlane;
+                const uint32_t a_hi = smem_u32(s.a[st]), a_lo = a_hi + kGPlaneA;
+                const uint32_t x_hi = smem_u32(s.x[st]), x_lo = x_hi + kGPlaneX;
 #pragma unroll
                 for (int kk = 0; kk < kGKS / 16; ++kk) {
                     const uint32_t o = kk * 32;
@@ -207,7 +217,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                 const __half* ws = reinterpret_cast<const __half*>(s.w[st] + kGM * kGKS) + r * 2;
                 const float s0 = __half2float(ws[0]) * pw, s1 = __half2float(ws[1]) * pw;
                 uint8_t* ahi = s.a[st];
-                uint8_t* alo = s.a[st] + kGPlane;
+                uint8_t* alo = s.a[st] + kGPlaneA;
 #pragma unroll
                 for (int ch = 0; ch < 8; ++ch) {  // 8 columns per 16-byte chunk
                     const uint2 qv = *reinterpret_cast<const uint2*>(wq + ch * 8);
@@ -238,12 +248,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         const int n = rt * kGM + row;
         const float inv_w = 1.0f / p.w_pow2[rt * kGM + row];
         if (acc_ok) {
-            for (int c0 = 0; c0 < kGNT; c0 += 16) {
+            for (int c0 = 0; c0 < NT; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int t = tt * kGNT + c0 + j;
+                    const int t = tt * NT + c0 + j;
                     if (t < p.tokens && n < p.n)
                         p.y[(static_cast<size_t>(split) * p.tokens + t) * p.y_ld + n] =
                             __uint_as_float(v[j]) * s.inv_x[c0 + j] * inv_w;
@@ -254,7 +264,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     tc_fence_before();
     __syncthreads();
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                                "r"(static_cast<uint32_t>(kGNT)));
+                                "r"(static_cast<uint32_t>(NT)));
 }
 
 // ---- layouts -----------------------------------------------------------------
@@ -297,14 +307,15 @@ __global__ void gemm_repack_kernel(const uint8_t* __restrict__ blocks, int64_t n
 }
 
 // Activations X [tokens][k] f32 -> [token tile][k step] planes (hi | lo,
-// 128B-swizzled, 128 tokens x 64 columns each) and 2^-kx per token, one warp
+// 128B-swizzled, nt tokens x 64 columns each) and 2^-kx per token, one warp
 // per token (tile rows past `tokens` are zero).
 __global__ void gemm_x_planes_kernel(const float* __restrict__ x, int64_t tokens, int64_t k, int64_t tokens_pad,
-                                     uint8_t* __restrict__ planes, float* __restrict__ inv) {
+                                     int nt, uint8_t* __restrict__ planes, float* __restrict__ inv) {
     const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (t >= tokens_pad) return;
-    const int64_t nks = k / kGKS, ttile = t / kGNT, tr = t % kGNT;
+    const int64_t plane = static_cast<int64_t>(nt) * kGKS * 2;
+    const int64_t nks = k / kGKS, ttile = t / nt, tr = t % nt;
     const float* row = x + t * k;
     float mx = 0.f;
     if (t < tokens)
@@ -328,10 +339,10 @@ __global__ void gemm_x_planes_kernel(const float* __restrict__ x, int64_t tokens
             hi[j] = __float2half_rn(v);
             lo[j] = __float2half_rn(v - __half2float(hi[j]));
         }
-        uint8_t* base = planes + (ttile * nks + ks) * (2 * kGPlane);
+        uint8_t* base = planes + (ttile * nks + ks) * (2 * plane);
         const uint32_t off = sw128_offset(static_cast<int>(tr), static_cast<int>(cc));
         *reinterpret_cast<uint4*>(base + off) = *reinterpret_cast<const uint4*>(hi);
-        *reinterpret_cast<uint4*>(base + kGPlane + off) = *reinterpret_cast<const uint4*>(lo);
+        *reinterpret_cast<uint4*>(base + plane + off) = *reinterpret_cast<const uint4*>(lo);
     }
     if (lane == 0) inv[t] = isx;
 }
@@ -353,10 +364,17 @@ int64_t gemm_q8_weight_bytes(int64_t n, int64_t k) {
     return ((n + kGM - 1) / kGM) * (k / kGKS) * kGWBytes;
 }
 int64_t gemm_q8_rows_padded(int64_t n) { return (n + kGM - 1) / kGM * kGM; }
+// Token tile of a matmul over `tokens` activation rows: 64 for small batches
+// (decode), else 256.
+int gemm_token_tile(int64_t tokens) { return tokens <= 64 ? 64 : 256; }
 int64_t gemm_x_plane_bytes(int64_t tokens, int64_t k) {
-    return ((tokens + kGNT - 1) / kGNT) * (k / kGKS) * 2 * kGPlane;
+    const int nt = gemm_token_tile(tokens);
+    return ((tokens + nt - 1) / nt) * (k / kGKS) * 2 * (static_cast<int64_t>(nt) * kGKS * 2);
 }
-int64_t gemm_tokens_padded(int64_t tokens) { return (tokens + kGNT - 1) / kGNT * kGNT; }
+int64_t gemm_tokens_padded(int64_t tokens) {
+    const int nt = gemm_token_tile(tokens);
+    return (tokens + nt - 1) / nt * nt;
+}
 
 int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out, float* pow2, void* stream) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -378,7 +396,7 @@ int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out
 int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream) {
     const int64_t tp = gemm_tokens_padded(tokens);
     gemm_x_planes_kernel<<<static_cast<unsigned>((tp + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        x, tokens, k, tp, planes, inv);
+        x, tokens, k, tp, gemm_token_tile(tokens), planes, inv);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -391,11 +409,15 @@ int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes,
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured != dev) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kGSmemBytes));
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(sizeof(GemmSmem<64>) + 1024));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_q8_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(sizeof(GemmSmem<256>) + 1024));
         if (e != cudaSuccess) return static_cast<int>(e);
         configured = dev;
     }
+    const int nt = gemm_token_tile(tokens);
     const int nks = static_cast<int>(k / kGKS);
     if (splits < 1) splits = 1;
     if (splits > nks) splits = nks;
@@ -413,10 +435,13 @@ int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes,
     p.y = splits > 1 ? part : y;
     p.err = err;
     p.timeout_ns = timeout_ns;
-    const dim3 grid(static_cast<unsigned>((n + kGM - 1) / kGM), static_cast<unsigned>((tokens + kGNT - 1) / kGNT),
+    const dim3 grid(static_cast<unsigned>((n + kGM - 1) / kGM), static_cast<unsigned>((tokens + nt - 1) / nt),
                     static_cast<unsigned>(splits));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    gemm_q8_kernel<<<grid, kGThreads, kGSmemBytes, st>>>(p);
+    if (nt == 64)
+        gemm_q8_kernel<64><<<grid, kGThreads, sizeof(GemmSmem<64>) + 1024, st>>>(p);
+    else
+        gemm_q8_kernel<256><<<grid, kGThreads, sizeof(GemmSmem<256>) + 1024, st>>>(p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || splits == 1) return static_cast<int>(e);
     const int64_t total = tokens * n;

@@ -137,6 +137,7 @@ SIGNATURES = {
 }
 
 _lib = None
+_FINALIZERS = {}
 
 
 def lib():
@@ -151,6 +152,8 @@ def lib():
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
+        for name in ("tir_gguf_close", "tir_model_destroy", "tir_state_destroy", "tir_batch_destroy"):
+            _FINALIZERS[name] = getattr(L, name)
         _lib = L
     return _lib
 
@@ -223,7 +226,8 @@ class GGUF:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().tir_gguf_close(self._h)
+            # bound at import time: finalizers may run after module teardown
+            _FINALIZERS["tir_gguf_close"](self._h)
             self._h = None
 
     def __del__(self):
@@ -324,7 +328,8 @@ class Model:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().tir_model_destroy(self._h)
+            # bound at import time: finalizers may run after module teardown
+            _FINALIZERS["tir_model_destroy"](self._h)
             self._h = None
 
     def __del__(self):
@@ -353,7 +358,8 @@ class State:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().tir_state_destroy(self._h)
+            # bound at import time: finalizers may run after module teardown
+            _FINALIZERS["tir_state_destroy"](self._h)
             self._h = None
 
     def __del__(self):
@@ -457,7 +463,8 @@ class Batch:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().tir_batch_destroy(self._h)
+            # bound at import time: finalizers may run after module teardown
+            _FINALIZERS["tir_batch_destroy"](self._h)
             self._h = None
 
     def __del__(self):
