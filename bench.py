@@ -176,6 +176,14 @@ def algorithmic_bytes(info, weight_bytes, n_forwards):
     return total
 
 
+def host_threads():
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def run_reference(args, dist):
     """The oracle (C restatement of the reference's Rayon path) on host cores."""
     import numpy as np
@@ -185,6 +193,7 @@ def run_reference(args, dist):
 
     path = synth.synthetic_model("tinyllama", args.seed)
     orc = load_oracle()
+    orc.set_threads(host_threads())  # torchrun sets OMP_NUM_THREADS=1; use every host core
     om = orc.model(GGUF(path))
     prompt = synth.prompt_ids(args.prompt, 32000, seed=args.seed)
     # bounded sample per step: 4 forwards (2 prompt ids + 2 greedy) at the
@@ -217,6 +226,7 @@ def cpu_baseline(args):
     from tir import synth
     path = synth.synthetic_model("tinyllama", args.seed)
     orc = load_oracle()
+    orc.set_threads(host_threads())
     om = orc.model(GGUF(path))
     prompt = synth.prompt_ids(args.prompt, 32000, seed=args.seed)
     om.generate_capped(prompt[:1], 0)  # page the weights in
