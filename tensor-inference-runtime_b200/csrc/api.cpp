@@ -1030,21 +1030,15 @@ tir_status tir_q8_matmul_batch(const float* x, int64_t tokens, const uint8_t* w,
     if (!c) return fail(TIR_ERR_OOM, "device context allocation failed");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int sms = decode_grid_size(dev);
-    const int64_t tiles = ((n + 127) / 128) * ((tokens + 127) / 128);
-    int splits = 1;
-    if (tiles < sms) splits = static_cast<int>(std::min<int64_t>(k / 64, std::max<int64_t>(1, sms / tiles)));
+    const int splits = gemm_splits(n, k, tokens, sms);
     uint8_t* planes = nullptr;
-    float* inv = nullptr;
-    float* part = nullptr;
     const size_t pbytes = static_cast<size_t>(gemm_x_plane_bytes(tokens, k));
     const size_t ibytes = static_cast<size_t>(gemm_tokens_padded(tokens)) * 4;
-    const size_t sbytes = splits > 1 ? static_cast<size_t>(splits) * tokens * n * 4 : 0;
-    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&planes), pbytes + ibytes + sbytes, st), "batched matmul scratch");
-    inv = reinterpret_cast<float*>(planes + pbytes);
-    part = splits > 1 ? reinterpret_cast<float*>(planes + pbytes + ibytes) : nullptr;
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&planes), pbytes + ibytes, st), "batched matmul scratch");
+    float* inv = reinterpret_cast<float*>(planes + pbytes);
     int rc = launch_gemm_x_planes(x, tokens, k, planes, inv, stream);
     if (rc == 0)
-        rc = launch_gemm_q8(w, w_pow2, planes, inv, n, k, tokens, y, n, splits, part, c->error, timeout_ns(), stream);
+        rc = launch_gemm_q8(w, w_pow2, planes, inv, n, k, tokens, y, n, 0, splits, c->error, timeout_ns(), stream);
     cudaFreeAsync(planes, st);
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "batched q8 matmul");
     return TIR_OK;

@@ -14,6 +14,8 @@
 #include <vector>
 
 #include "host.h"
+#include "launch.cuh"
+#include "ptx.cuh"
 #include "runtime.h"
 
 namespace tir {
@@ -21,7 +23,6 @@ namespace {
 
 constexpr uint32_t kBErrBadToken = 12;
 constexpr int kQBlock = 32;   // query tokens per prefill attention CTA (one per lane)
-constexpr int kKChunk = 32;   // key positions staged per step
 
 // Q8_0 blocks of a matrix held in the decode kernel's warp-sliced tile-major
 // layout (runtime.h q8_slice_offset), written back as [n][k/32] 34-byte blocks.
@@ -50,6 +51,8 @@ __global__ void tiled_to_blocks_kernel(const uint8_t* __restrict__ tiled, int64_
 __global__ void embed_rows_kernel(const int32_t* __restrict__ ids, const uint8_t* __restrict__ eq,
                                   const uint16_t* __restrict__ es, int64_t esk, int H, int vocab,
                                   float* __restrict__ X, uint32_t* err) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t t = blockIdx.x;
     int id = ids[t];
     if (id < 0 || id >= vocab) {
@@ -62,34 +65,17 @@ __global__ void embed_rows_kernel(const int32_t* __restrict__ ids, const uint8_t
     }
 }
 
-// out[i] = rmsnorm(X[rows ? rows[i] : i]) * w  (src/math.rs:141-150; the
-// division as a multiplication by the correctly rounded reciprocal).
-__global__ void rmsnorm_rows_kernel(const float* __restrict__ X, const int32_t* __restrict__ rows, int H,
-                                    const float* __restrict__ w, float eps, float* __restrict__ out) {
-    __shared__ float red[32];
-    const int64_t r = rows ? rows[blockIdx.x] : blockIdx.x;
-    const float* x = X + r * H;
-    float ss = 0.f;
-    for (int c = threadIdx.x; c < H; c += blockDim.x) ss = fmaf(x[c], x[c], ss);
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float total = 0.f;
-    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) total += red[i];
-    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(H)), eps)));
-    float* o = out + static_cast<int64_t>(blockIdx.x) * H;
-    for (int c = threadIdx.x; c < H; c += blockDim.x) o[c] = __fmul_rn(__fmul_rn(x[c], w[c]), inv);
-}
-
 // RoPE on the q and k parts of each token's fused q|k|v row (src/math.rs:196-228),
 // then the KV-cache append (src/forward.rs:83-84).  Token t belongs to
-// sequence t / tps at position pos0 + t % tps; cache [seq][max_ctx][kvd].
-__global__ void rope_append_kernel(float* __restrict__ qkv, int64_t ld, int tps, int pos0, int H, int kvd,
+// sequence t / tps at position *pos0 + t % tps; cache [seq][max_ctx][kvd].
+__global__ void rope_append_kernel(float* __restrict__ qkv, int64_t ld, int tps, const int32_t* pos0, int H, int kvd,
                                    int max_ctx, const float* __restrict__ rc, const float* __restrict__ rs,
                                    float* __restrict__ kc, float* __restrict__ vc) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t t = blockIdx.x;
     const int64_t s = t / tps;
-    const int pos = pos0 + static_cast<int>(t % tps);
+    const int pos = *pos0 + static_cast<int>(t % tps);
     float* row = qkv + t * ld;
     const size_t cache_row = (static_cast<size_t>(s) * max_ctx + pos) * kvd;
     for (int pr = threadIdx.x; pr < (H + kvd) / 2; pr += blockDim.x) {
@@ -113,20 +99,31 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int64_t ld, int tps,
 
 // Causal grouped-query attention for tps >= 2 new tokens per sequence
 // (src/forward.rs:79-174 for every query position): CTA per (sequence, kv
-// head, block of 32 query tokens); warp h handles query head g * group + h,
-// lane i query token i of the block, with its q and running output in
-// registers; keys are staged 32 positions at a time in shared memory.  Online
-// softmax (running max and sum), scale 1/sqrt(64).
-__global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t ld, int tps, int pos0, int H, int kvd,
-                                    int group, int max_ctx, const float* __restrict__ kc,
-                                    const float* __restrict__ vc, float* __restrict__ out) {
-    __shared__ float ks[kKChunk][kHeadDim];
-    __shared__ float vs[kKChunk][kHeadDim];
-    const int s = blockIdx.x, g = blockIdx.y, qb = blockIdx.z;
+// head and group of up to kPHeads of its query heads, block of 32 query
+// tokens); warp w handles one query head, lane i query token i of the block, with its q and running output in
+// registers; keys are staged kPChunk positions at a time in shared memory and
+// taken four at a time (four independent score chains, one running-max
+// update per four keys).  Online softmax (running max and sum), scale
+// 1/sqrt(64).
+constexpr int kPChunk = 64;
+constexpr int kPHeads = 8;  // query heads (warps) per CTA
+
+__global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const float* __restrict__ qkv, int64_t ld, int tps,
+                                                              const int32_t* pos0p, int H, int kvd, int group,
+                                                              int max_ctx, const float* __restrict__ kc,
+                                                              const float* __restrict__ vc, float* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ __align__(16) float4 ks[kPChunk][kHeadDim / 4];
+    __shared__ __align__(16) float4 vs[kPChunk][kHeadDim / 4];
+    const int n_hb = (group + kPHeads - 1) / kPHeads;
+    const int s = blockIdx.x, g = blockIdx.y / n_hb, hb = blockIdx.y % n_hb, qb = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = g * group + warp;
+    const int hg = hb * kPHeads + warp;  // query head within the group
+    const int h = g * group + hg;
     const int qi = qb * kQBlock + lane;  // query token within the sequence's new tokens
-    const bool active = qi < tps && warp < group;
+    const bool active = qi < tps && hg < group;
+    const int pos0 = *pos0p;
     const int qpos = pos0 + qi;
     const int64_t t = static_cast<int64_t>(s) * tps + qi;
     float q[kHeadDim], o[kHeadDim];
@@ -138,33 +135,87 @@ __global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t ld, i
     float m = -INFINITY, l = 0.f;
     const int last = pos0 + min(tps, (qb + 1) * kQBlock) - 1;  // the block's last query position
     const size_t head_base = static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
-    for (int c0 = 0; c0 <= last; c0 += kKChunk) {
+    for (int c0 = 0; c0 <= last; c0 += kPChunk) {
         __syncthreads();
-        for (int e = threadIdx.x; e < kKChunk * kHeadDim; e += blockDim.x) {
-            const int j = e / kHeadDim, d = e % kHeadDim;
+        for (int e = threadIdx.x; e < kPChunk * (kHeadDim / 4); e += blockDim.x) {
+            const int j = e / (kHeadDim / 4), d4 = e % (kHeadDim / 4);
             const bool in = c0 + j <= last;
-            ks[j][d] = in ? kc[head_base + static_cast<size_t>(c0 + j) * kvd + d] : 0.f;
-            vs[j][d] = in ? vc[head_base + static_cast<size_t>(c0 + j) * kvd + d] : 0.f;
+            const size_t off = head_base + static_cast<size_t>(c0 + j) * kvd;
+            ks[j][d4] = in ? reinterpret_cast<const float4*>(kc + off)[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
+            vs[j][d4] = in ? reinterpret_cast<const float4*>(vc + off)[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         __syncthreads();
-        if (active) {
-            const int jmax = min(kKChunk, qpos - c0 + 1);
-            for (int j = 0; j < jmax; ++j) {
-                float acc = 0.f;
+        if (!active) continue;
+        const int jmax = min(kPChunk, qpos - c0 + 1);
+        int j = 0;
+        for (; j + 4 <= jmax; j += 4) {
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int d = 0; d < kHeadDim; ++d) acc = fmaf(q[d], ks[j][d], acc);
-                const float sc = acc / 8.0f;  // sqrt(64)
-                if (sc > m) {
-                    const float corr = expf(m - sc);
-                    l *= corr;
+            for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
 #pragma unroll
-                    for (int d = 0; d < kHeadDim; ++d) o[d] *= corr;
-                    m = sc;
+                for (int u = 0; u < 4; ++u) {
+                    const float4 kv = ks[j + u][d4];
+                    sc[u] = fmaf(q[4 * d4], kv.x, sc[u]);
+                    sc[u] = fmaf(q[4 * d4 + 1], kv.y, sc[u]);
+                    sc[u] = fmaf(q[4 * d4 + 2], kv.z, sc[u]);
+                    sc[u] = fmaf(q[4 * d4 + 3], kv.w, sc[u]);
                 }
-                const float pj = expf(sc - m);
-                l += pj;
+            }
 #pragma unroll
-                for (int d = 0; d < kHeadDim; ++d) o[d] = fmaf(pj, vs[j][d], o[d]);
+            for (int u = 0; u < 4; ++u) sc[u] = sc[u] / 8.0f;  // sqrt(64)
+            const float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+            if (mx > m) {
+                const float corr = expf(m - mx);
+                l *= corr;
+#pragma unroll
+                for (int d = 0; d < kHeadDim; ++d) o[d] *= corr;
+                m = mx;
+            }
+            float pj[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                pj[u] = expf(sc[u] - m);
+                l += pj[u];
+            }
+#pragma unroll
+            for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 vv = vs[j + u][d4];
+                    o[4 * d4] = fmaf(pj[u], vv.x, o[4 * d4]);
+                    o[4 * d4 + 1] = fmaf(pj[u], vv.y, o[4 * d4 + 1]);
+                    o[4 * d4 + 2] = fmaf(pj[u], vv.z, o[4 * d4 + 2]);
+                    o[4 * d4 + 3] = fmaf(pj[u], vv.w, o[4 * d4 + 3]);
+                }
+            }
+        }
+        for (; j < jmax; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
+                const float4 kv = ks[j][d4];
+                acc = fmaf(q[4 * d4], kv.x, acc);
+                acc = fmaf(q[4 * d4 + 1], kv.y, acc);
+                acc = fmaf(q[4 * d4 + 2], kv.z, acc);
+                acc = fmaf(q[4 * d4 + 3], kv.w, acc);
+            }
+            const float sc = acc / 8.0f;
+            if (sc > m) {
+                const float corr = expf(m - sc);
+                l *= corr;
+#pragma unroll
+                for (int d = 0; d < kHeadDim; ++d) o[d] *= corr;
+                m = sc;
+            }
+            const float pj = expf(sc - m);
+            l += pj;
+#pragma unroll
+            for (int d4 = 0; d4 < kHeadDim / 4; ++d4) {
+                const float4 vv = vs[j][d4];
+                o[4 * d4] = fmaf(pj, vv.x, o[4 * d4]);
+                o[4 * d4 + 1] = fmaf(pj, vv.y, o[4 * d4 + 1]);
+                o[4 * d4 + 2] = fmaf(pj, vv.z, o[4 * d4 + 2]);
+                o[4 * d4 + 3] = fmaf(pj, vv.w, o[4 * d4 + 3]);
             }
         }
     }
@@ -175,84 +226,124 @@ __global__ void attn_prefill_kernel(const float* __restrict__ qkv, int64_t ld, i
     }
 }
 
-// One new token per sequence (decode): CTA per (sequence, kv head), warp h
-// for query head g * group + h, lanes over key positions for the scores and
-// over dimensions (two each) for the output; keys staged 32 at a time.
-__global__ void attn_decode_kernel(const float* __restrict__ qkv, int64_t ld, int pos, int H, int kvd, int group,
-                                   int max_ctx, const float* __restrict__ kc, const float* __restrict__ vc,
-                                   float* __restrict__ out) {
-    __shared__ float ks[kKChunk][kHeadDim + 1];
-    __shared__ float vs[kKChunk][kHeadDim];
-    __shared__ float qs[16][kHeadDim];
+// One new token per sequence (decode), src/forward.rs:79-174: CTA per
+// (sequence, kv head) with kAttnWarps warps splitting the key positions in
+// chunks of 32 (warp w takes chunks w, w + kAttnWarps, ...).  Lane j scores
+// key j of its chunk against every query head of the group (queries in
+// shared memory), the warp folds the chunk into a running (max, sum, output)
+// per head with lanes over output dimensions, and the warps' states merge at
+// the end.  Scale 1/sqrt(64), softmax with the running-max shift.
+constexpr int kAttnWarps = 8;
+
+template <int G>  // query heads per kv head, rounded up (heads >= group are computed on zeros, not stored)
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const float* __restrict__ qkv, int64_t ld,
+                                                                      const int32_t* posp, int H, int kvd, int group,
+                                                                      int max_ctx,
+                                                                      const float* __restrict__ kc,
+                                                                      const float* __restrict__ vc,
+                                                                      float* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ __align__(16) float qs[G][kHeadDim];
+    __shared__ float ms[kAttnWarps][G], ls[kAttnWarps][G];
+    __shared__ float os[kAttnWarps][G][kHeadDim];
     const int s = blockIdx.x, g = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = g * group + warp;
-    const bool active = warp < group;
-    for (int e = threadIdx.x; e < group * kHeadDim; e += blockDim.x)
-        qs[e / kHeadDim][e % kHeadDim] = qkv[static_cast<int64_t>(s) * ld + (g * group) * kHeadDim + e];
-    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
-    const size_t head_base = static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
-    for (int c0 = 0; c0 <= pos; c0 += kKChunk) {
-        __syncthreads();
-        const int nc = min(kKChunk, pos - c0 + 1);
-        for (int e = threadIdx.x; e < kKChunk * kHeadDim; e += blockDim.x) {
-            const int j = e / kHeadDim, d = e % kHeadDim;
-            const bool in = j < nc;
-            ks[j][d] = in ? kc[head_base + static_cast<size_t>(c0 + j) * kvd + d] : 0.f;
-            vs[j][d] = in ? vc[head_base + static_cast<size_t>(c0 + j) * kvd + d] : 0.f;
-        }
-        __syncthreads();
-        if (active) {
-            float sc = -INFINITY;
-            if (lane < nc) {
-                float acc = 0.f;
-#pragma unroll 16
-                for (int d = 0; d < kHeadDim; ++d) acc = fmaf(qs[warp][d], ks[lane][d], acc);
-                sc = acc / 8.0f;
+    for (int e = threadIdx.x; e < G * kHeadDim; e += blockDim.x)
+        qs[e / kHeadDim][e % kHeadDim] =
+            e / kHeadDim < group ? qkv[static_cast<int64_t>(s) * ld + (g * group) * kHeadDim + e] : 0.f;
+    __syncthreads();
+    float m[G], l[G], o0[G], o1[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+        o0[h] = 0.f;
+        o1[h] = 0.f;
+    }
+    const int n = *posp + 1;
+    const float* kb = kc + static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
+    const float* vb = vc + static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
+    for (int c0 = warp * 32; c0 < n; c0 += kAttnWarps * 32) {
+        const int j = c0 + lane;
+        const bool valid = j < n;
+        float p[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) p[h] = 0.f;
+        const float4* kr = reinterpret_cast<const float4*>(kb + static_cast<size_t>(valid ? j : c0) * kvd);
+#pragma unroll 4
+        for (int i = 0; i < kHeadDim / 4; ++i) {
+            const float4 kv = kr[i];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float4 qv = reinterpret_cast<const float4*>(qs[h])[i];
+                p[h] = fmaf(qv.x, kv.x, p[h]);
+                p[h] = fmaf(qv.y, kv.y, p[h]);
+                p[h] = fmaf(qv.z, kv.z, p[h]);
+                p[h] = fmaf(qv.w, kv.w, p[h]);
             }
-            float mx = sc;
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) p[h] = valid ? p[h] / 8.0f : -INFINITY;  // sqrt(64)
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+            float mx = p[h];
+#pragma unroll
             for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float m_new = fmaxf(m, mx);
-            const float pj = lane < nc ? expf(sc - m_new) : 0.f;
+            const float m_new = fmaxf(m[h], mx);  // finite: lane 0 of the chunk is a valid key
+            const float pj = valid ? expf(p[h] - m_new) : 0.f;
             float ps = pj;
+#pragma unroll
             for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-            const float corr = expf(m - m_new);
-            l = l * corr + ps;
-            o0 *= corr;
-            o1 *= corr;
-            for (int j = 0; j < nc; ++j) {
-                const float pt = __shfl_sync(0xffffffffu, pj, j);
-                o0 = fmaf(pt, vs[j][lane], o0);
-                o1 = fmaf(pt, vs[j][lane + 32], o1);
+            const float corr = expf(m[h] - m_new);
+            l[h] = l[h] * corr + ps;
+            o0[h] *= corr;
+            o1[h] *= corr;
+            m[h] = m_new;
+            p[h] = pj;
+        }
+        const int nc = min(32, n - c0);
+        for (int jj = 0; jj < nc; ++jj) {
+            const float* vr = vb + static_cast<size_t>(c0 + jj) * kvd;
+            const float v0 = vr[lane], v1 = vr[lane + 32];
+#pragma unroll
+            for (int h = 0; h < G; ++h) {
+                const float pt = __shfl_sync(0xffffffffu, p[h], jj);
+                o0[h] = fmaf(pt, v0, o0[h]);
+                o1[h] = fmaf(pt, v1, o1[h]);
             }
-            m = m_new;
         }
     }
-    if (active) {
-        out[static_cast<int64_t>(s) * H + h * kHeadDim + lane] = o0 / l;
-        out[static_cast<int64_t>(s) * H + h * kHeadDim + lane + 32] = o1 / l;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+        if (lane == 0) {
+            ms[warp][h] = m[h];
+            ls[warp][h] = l[h];
+        }
+        os[warp][h][lane] = o0[h];
+        os[warp][h][lane + 32] = o1[h];
     }
-}
-
-__global__ void residual_add_kernel(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        x[i] = __fadd_rn(x[i], y[i]);
-}
-
-// h[t][j] = silu(gate) * up from interleaved (gate_j, up_j) columns
-// (src/math.rs:171-175).
-__global__ void silu_pairs_kernel(const float* __restrict__ gu, int64_t tokens, int F, float* __restrict__ h) {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < tokens * F;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t t = i / F, j = i % F;
-        const float g = gu[t * 2 * F + 2 * j], u = gu[t * 2 * F + 2 * j + 1];
-        h[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    __syncthreads();
+    for (int e = threadIdx.x; e < group * kHeadDim; e += blockDim.x) {
+        const int h = e / kHeadDim, d = e % kHeadDim;
+        float mx = ms[0][h];
+#pragma unroll
+        for (int w = 1; w < kAttnWarps; ++w) mx = fmaxf(mx, ms[w][h]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = expf(ms[w][h] - mx);  // 0 for a warp that had no keys
+            L = fmaf(ls[w][h], f, L);
+            O = fmaf(os[w][h][d], f, O);
+        }
+        out[static_cast<int64_t>(s) * H + (g * group + h) * kHeadDim + d] = O / L;
     }
 }
 
 // Greedy sample per row (src/tokenizer.rs:152-167: total order, ties -> last).
 __global__ void argmax_rows_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out) {
+    griddep_launch_dependents();
+    griddep_wait();
     __shared__ unsigned long long red[32];
     const float* r = x + static_cast<int64_t>(blockIdx.x) * n;
     unsigned long long best = 0ull;
@@ -271,9 +362,27 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int64_t n, int32
     }
 }
 
-__global__ void last_rows_kernel(int32_t* rows, int n_seqs, int tps) {
+// Each sequence's last new row; the device length advances by tps (every
+// kernel of the forward that reads it has run by now).
+__global__ void last_rows_kernel(int32_t* rows, int n_seqs, int tps, int32_t* len) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s < n_seqs) rows[s] = s * tps + tps - 1;
+    if (s == 0) *len += tps;
+}
+
+// Greedy decode feedback: the sampled ids are both the next input and
+// generated output.
+__global__ void feed_kernel(const int32_t* __restrict__ next, int32_t* __restrict__ ids, int32_t* __restrict__ gen,
+                            int n_seqs) {
+    griddep_launch_dependents();
+    griddep_wait();
+    for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < n_seqs; s += gridDim.x * blockDim.x) {
+        const int32_t v = next[s];
+        ids[s] = v;
+        gen[s] = v;
+    }
 }
 
 unsigned g1(int64_t n, int threads) { return static_cast<unsigned>(std::min<int64_t>((n + threads - 1) / threads, 148 * 16)); }
@@ -296,15 +405,19 @@ struct tir_batch {
     std::vector<GW> qkv, o, gu, down;
     GW lm;
     float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr;
-    float *X = nullptr, *XN = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *HH = nullptr, *Y = nullptr,
-          *LG = nullptr, *inv = nullptr, *part = nullptr;
+    float *X = nullptr, *Y = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *LG = nullptr, *inv = nullptr;
     uint8_t* planes = nullptr;
     int32_t *ids = nullptr, *rows = nullptr, *next = nullptr, *h_next = nullptr;
     uint32_t *err = nullptr, *h_err = nullptr;
-    size_t part_floats = 0;
+    int32_t* len_dev = nullptr;  // the sequences' length on the device (kernels read it: graph replays stay valid)
+    int32_t* gen = nullptr;      // generated ids [gen_cap][B] (tir_batch_generate)
+    int gen_cap = 0;
+    cudaGraphExec_t decode_graph = nullptr;  // one decode forward (tps = 1) + id feedback, captured on first use
     ~tir_batch() {
         cudaSetDevice(m ? m->device : 0);
         if (stream) cudaStreamSynchronize(stream);
+        if (decode_graph) cudaGraphExecDestroy(decode_graph);
+        if (gen) cudaFree(gen);
         for (void* p : allocs) cudaFree(p);
         if (h_next) cudaFreeHost(h_next);
         if (h_err) cudaFreeHost(h_err);
@@ -343,23 +456,47 @@ tir_status make_gw(tir_batch* b, const Mat& mt, uint8_t* staging, tir_batch::GW&
     return TIR_OK;
 }
 
-tir_status gemm(tir_batch* b, const float* x, int64_t tokens, const tir_batch::GW& g, float* y) {
-    int rc = launch_gemm_x_planes(x, tokens, g.k, b->planes, b->inv, b->stream);
-    if (rc != 0) return bfail(static_cast<cudaError_t>(rc), "activation planes");
-    const int64_t tiles = ((g.n + 127) / 128) * ((tokens + 127) / 128);
-    int splits = 1;
-    if (tiles < b->sms && tokens <= 256) {
-        splits = static_cast<int>(std::min<int64_t>(g.k / 64, std::max<int64_t>(1, b->sms / tiles)));
-        while (splits > 1 && static_cast<size_t>(splits) * tokens * g.n > b->part_floats) --splits;
-    }
-    rc = launch_gemm_q8(g.w, g.p2, b->planes, b->inv, g.n, g.k, tokens, y, g.n, splits, b->part, b->err,
-                        2000ull * 1000000ull, b->stream);
+// y (row stride g.n) = the matmul of the activation planes in b->planes (as
+// written for `tokens` rows) with g, or y += it when accumulate.
+tir_status mm(tir_batch* b, int64_t tokens, const tir_batch::GW& g, float* y, bool accumulate) {
+    const int splits = gemm_splits(g.n, g.k, tokens, b->sms);
+    const int rc = launch_gemm_q8(g.w, g.p2, b->planes, b->inv, g.n, g.k, tokens, y, g.n, accumulate ? 1 : 0, splits,
+                                  b->err, 2000ull * 1000000ull, b->stream, true);
     if (rc != 0) return bfail(static_cast<cudaError_t>(rc), "tensor-core matmul");
     return TIR_OK;
 }
 
+tir_status planes_rc(int rc) {
+    return rc == 0 ? TIR_OK : bfail(static_cast<cudaError_t>(rc), "activation planes");
+}
+
+// Decode attention over the group size rounded up to an instantiated width.
+void attn_decode(tir_batch* b, int group, int kv_heads, int H, int KVD, int64_t ldq, const float* kc,
+                 const float* vc) {
+    const dim3 grid(static_cast<unsigned>(b->B), static_cast<unsigned>(kv_heads));
+    const unsigned th = kAttnWarps * 32;
+#define TIR_ATTN(GM) \
+    launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, ldq, b->len_dev, H, KVD, group, \
+                  b->max_ctx, kc, vc, b->ATT)
+    if (group <= 1)
+        TIR_ATTN(1);
+    else if (group <= 2)
+        TIR_ATTN(2);
+    else if (group <= 4)
+        TIR_ATTN(4);
+    else if (group <= 8)
+        TIR_ATTN(8);
+    else
+        TIR_ATTN(16);
+#undef TIR_ATTN
+}
+
 // One forward over tps new tokens of every sequence (ids already in b->ids,
-// sequence-major); greedy next id of every sequence into b->next.
+// sequence-major); greedy next id of every sequence into b->next.  Per
+// layer: the previous layer's residual add + rmsnorm fused into the
+// activation planes of the q|k|v matmul, RoPE + KV append, attention, the o
+// matmul (into Y), residual add + rmsnorm into the gate|up planes, SiLU * up
+// into the down planes, the down matmul (into Y, added by the next norm).
 tir_status forward(tir_batch* b, int tps) {
     tir_model* m = b->m;
     const tir_transformer& t = m->t;
@@ -371,54 +508,102 @@ tir_status forward(tir_batch* b, int tps) {
     const size_t layer_cache = static_cast<size_t>(b->B) * b->max_ctx * KVD;
     cudaStream_t st = b->stream;
     tir_status rc;
-    embed_rows_kernel<<<static_cast<unsigned>(T), 256, 0, st>>>(b->ids, m->embd.q, m->embd.s, m->embd.sk, H, V, b->X,
-                                                                 b->err);
+    launch_kernel(embed_rows_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->ids, m->embd.q,
+                  m->embd.s, m->embd.sk, H, V, b->X, b->err);
     for (int l = 0; l < L; ++l) {
-        rmsnorm_rows_kernel<<<static_cast<unsigned>(T), 256, 0, st>>>(b->X, nullptr, H, m->attn_norm[l], 1e-5f, b->XN);
-        if ((rc = gemm(b, b->XN, T, b->qkv[l], b->QKV)) != TIR_OK) return rc;
+        // the residual add of the previous layer's down projection (none before layer 0)
+        if ((rc = planes_rc(launch_gemm_norm_planes(b->X, l > 0 ? b->Y : nullptr, nullptr, T, H, m->attn_norm[l],
+                                                    1e-5f, b->planes, b->inv, st, true))) != TIR_OK)
+            return rc;
+        if ((rc = mm(b, T, b->qkv[l], b->QKV, false)) != TIR_OK) return rc;
         float* kc = b->kc + l * layer_cache;
         float* vc = b->vc + l * layer_cache;
-        rope_append_kernel<<<static_cast<unsigned>(T), 256, 0, st>>>(b->QKV, ldq, tps, b->len, H, KVD, b->max_ctx,
-                                                                      b->rcos, b->rsin, kc, vc);
+        launch_kernel(rope_append_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->QKV, ldq, tps,
+                      b->len_dev, H, KVD, b->max_ctx, b->rcos, b->rsin, kc, vc);
         if (tps == 1) {
-            attn_decode_kernel<<<dim3(b->B, static_cast<unsigned>(t.k_v_heads)), group * 32, 0, st>>>(
-                b->QKV, ldq, b->len, H, KVD, group, b->max_ctx, kc, vc, b->ATT);
+            attn_decode(b, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);
         } else {
-            attn_prefill_kernel<<<dim3(b->B, static_cast<unsigned>(t.k_v_heads), (tps + kQBlock - 1) / kQBlock),
-                                  group * 32, 0, st>>>(b->QKV, ldq, tps, b->len, H, KVD, group, b->max_ctx, kc, vc,
-                                                       b->ATT);
+            launch_kernel(attn_prefill_kernel,
+                          dim3(b->B, static_cast<unsigned>(t.k_v_heads * ((group + kPHeads - 1) / kPHeads)),
+                               (tps + kQBlock - 1) / kQBlock),
+                          dim3(kPHeads * 32), 0, st, true, b->QKV, ldq, tps, b->len_dev, H, KVD, group, b->max_ctx, kc,
+                          vc, b->ATT);
         }
-        if ((rc = gemm(b, b->ATT, T, b->o[l], b->Y)) != TIR_OK) return rc;
-        residual_add_kernel<<<g1(T * H, 256), 256, 0, st>>>(b->X, b->Y, T * H);
-        rmsnorm_rows_kernel<<<static_cast<unsigned>(T), 256, 0, st>>>(b->X, nullptr, H, m->ffn_norm[l], 1e-5f, b->XN);
-        if ((rc = gemm(b, b->XN, T, b->gu[l], b->GU)) != TIR_OK) return rc;
-        silu_pairs_kernel<<<g1(T * F, 256), 256, 0, st>>>(b->GU, T, F, b->HH);
-        if ((rc = gemm(b, b->HH, T, b->down[l], b->Y)) != TIR_OK) return rc;
-        residual_add_kernel<<<g1(T * H, 256), 256, 0, st>>>(b->X, b->Y, T * H);
+        if ((rc = planes_rc(launch_gemm_x_planes(b->ATT, T, H, b->planes, b->inv, st, true))) != TIR_OK) return rc;
+        if ((rc = mm(b, T, b->o[l], b->Y, false)) != TIR_OK) return rc;
+        if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, nullptr, T, H, m->ffn_norm[l], 1e-5f, b->planes,
+                                                    b->inv, st, true))) != TIR_OK)
+            return rc;
+        if ((rc = mm(b, T, b->gu[l], b->GU, false)) != TIR_OK) return rc;
+        if ((rc = planes_rc(launch_gemm_silu_planes(b->GU, T, F, b->planes, b->inv, st, true))) != TIR_OK) return rc;
+        if ((rc = mm(b, T, b->down[l], b->Y, false)) != TIR_OK) return rc;
     }
-    last_rows_kernel<<<(b->B + 127) / 128, 128, 0, st>>>(b->rows, b->B, tps);
-    rmsnorm_rows_kernel<<<static_cast<unsigned>(b->B), 256, 0, st>>>(b->X, b->rows, H, m->out_norm, 1e-5f, b->XN);
-    if ((rc = gemm(b, b->XN, b->B, b->lm, b->LG)) != TIR_OK) return rc;
-    argmax_rows_kernel<<<static_cast<unsigned>(b->B), 256, 0, st>>>(b->LG, V, b->next);
+    launch_kernel(last_rows_kernel, dim3((b->B + 127) / 128), dim3(128), 0, st, true, b->rows, b->B, tps, b->len_dev);
+    // the last down projection's residual add, on the rows the logits need
+    if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, b->rows, b->B, H, m->out_norm, 1e-5f, b->planes, b->inv,
+                                                st, true))) != TIR_OK)
+        return rc;
+    if ((rc = mm(b, b->B, b->lm, b->LG, false)) != TIR_OK) return rc;
+    launch_kernel(argmax_rows_kernel, dim3(static_cast<unsigned>(b->B)), dim3(256), 0, st, true, b->LG,
+                  static_cast<int64_t>(V), b->next);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return bfail(e, "batched forward");
     b->len += tps;
     return TIR_OK;
 }
 
+// forward(b, 1) through a CUDA graph captured on first use: the launch
+// sequence of a decode step depends only on the batch's buffers, and every
+// kernel reads the position from the device.
+tir_status decode_forward(tir_batch* b) {
+    if (!b->decode_graph) {
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return bfail(e, "decode graph capture");
+        const int len0 = b->len;
+        const tir_status rc = forward(b, 1);
+        b->len = len0;  // the capture ran nothing
+        e = cudaStreamEndCapture(b->stream, &g);
+        if (rc != TIR_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return bfail(e, "decode graph capture");
+        e = cudaGraphInstantiate(&b->decode_graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+            b->decode_graph = nullptr;
+            return bfail(e, "decode graph instantiation");
+        }
+    }
+    const cudaError_t e = cudaGraphLaunch(b->decode_graph, b->stream);
+    if (e != cudaSuccess) return bfail(e, "decode graph launch");
+    b->len += 1;
+    return TIR_OK;
+}
+
+// Empty every sequence (host and device lengths).
+tir_status reset_len(tir_batch* b) {
+    b->len = 0;
+    const cudaError_t e = cudaMemsetAsync(b->len_dev, 0, 4, b->stream);
+    return e == cudaSuccess ? TIR_OK : bfail(e, "length reset");
+}
+
 tir_status check_err(tir_batch* b) {
     cudaError_t e = cudaMemcpyAsync(b->h_err, b->err, 4, cudaMemcpyDeviceToHost, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return bfail(e, "batched forward");
-    if (*b->h_err == kBErrBadToken) {
-        b->len = 0;
-        return fail(TIR_ERR_BAD_TOKEN, "a token id is not in the vocab; the batch was reset");
-    }
-    if (*b->h_err != 0) {
-        b->len = 0;
-        return fail(TIR_ERR_TIMEOUT, "device wait timed out; the batch was reset");
-    }
-    return TIR_OK;
+    const uint32_t code = *b->h_err;
+    if (code == 0) return TIR_OK;
+    // reset: sequences and the error word
+    b->len = 0;
+    *b->h_err = 0;
+    e = cudaMemsetAsync(b->err, 0, 16, b->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(b->len_dev, 0, 4, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return bfail(e, "batch reset");
+    if (code == kBErrBadToken) return fail(TIR_ERR_BAD_TOKEN, "a token id is not in the vocab; the batch was reset");
+    return fail(TIR_ERR_TIMEOUT, "device wait timed out; the batch was reset");
 }
 
 }  // namespace
@@ -452,17 +637,17 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
     const int64_t H = t.embed_dim, KVD = t.kv_dim, F = t.ffn_dim, V = t.vocab, L = t.layers;
     const int64_t T = static_cast<int64_t>(n_seqs) * max_tokens_per_seq;
     const int64_t kmax = std::max(H, F);
-    b->part_floats = static_cast<size_t>(b->sms) * 128 * 256;
     const size_t cache = static_cast<size_t>(L) * n_seqs * max_ctx * KVD;
     bool ok = balloc(b, cache * 4, &b->kc) && balloc(b, cache * 4, &b->vc) &&
               balloc(b, static_cast<size_t>(max_ctx) * 32 * 4, &b->rcos) &&
               balloc(b, static_cast<size_t>(max_ctx) * 32 * 4, &b->rsin) && balloc(b, T * H * 4, &b->X) &&
-              balloc(b, T * H * 4, &b->XN) && balloc(b, T * (H + 2 * KVD) * 4, &b->QKV) &&
-              balloc(b, T * H * 4, &b->ATT) && balloc(b, T * 2 * F * 4, &b->GU) && balloc(b, T * F * 4, &b->HH) &&
-              balloc(b, T * H * 4, &b->Y) && balloc(b, static_cast<size_t>(n_seqs) * V * 4, &b->LG) &&
+              balloc(b, T * H * 4, &b->Y) &&
+              balloc(b, T * (H + 2 * KVD) * 4, &b->QKV) && balloc(b, T * H * 4, &b->ATT) &&
+              balloc(b, T * 2 * F * 4, &b->GU) && balloc(b, static_cast<size_t>(n_seqs) * V * 4, &b->LG) &&
+              balloc(b, 16, &b->len_dev) &&
               balloc(b, static_cast<size_t>(gemm_x_plane_bytes(T, kmax)), &b->planes) &&
               balloc(b, static_cast<size_t>(gemm_tokens_padded(T)) * 4, &b->inv) &&
-              balloc(b, b->part_floats * 4, &b->part) && balloc(b, T * 4, &b->ids) &&
+              balloc(b, T * 4, &b->ids) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->rows) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->next) && balloc(b, 16, &b->err);
     if (!ok || cudaMallocHost(&b->h_next, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
@@ -474,7 +659,8 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
     rope_table(t.base_freq, kHeadDim, max_ctx, c, s);
     if (cudaMemcpy(b->rcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(b->rsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(b->err, 0, 16) != cudaSuccess) {
+        cudaMemset(b->err, 0, 16) != cudaSuccess ||
+        cudaMemset(b->len_dev, 0, 16) != cudaSuccess || gemm_configure() != 0) {
         delete b;
         return fail(TIR_ERR_CUDA, "batch initialisation failed");
     }
@@ -511,8 +697,8 @@ void tir_batch_destroy(tir_batch* b) { delete b; }
 
 tir_status tir_batch_reset(tir_batch* b) {
     if (!b) return fail(TIR_ERR_INVALID_ARG, "null argument");
-    b->len = 0;
-    return TIR_OK;
+    cudaSetDevice(b->m->device);
+    return reset_len(b);
 }
 
 int32_t tir_batch_len(const tir_batch* b) { return b ? b->len : 0; }
@@ -529,7 +715,7 @@ tir_status tir_batch_step(tir_batch* b, const int32_t* ids_host, int32_t tokens_
     const size_t n = static_cast<size_t>(b->B) * tokens_per_seq;
     cudaError_t e = cudaMemcpyAsync(b->ids, ids_host, n * 4, cudaMemcpyHostToDevice, b->stream);
     if (e != cudaSuccess) return bfail(e, "id upload");
-    tir_status rc = forward(b, tokens_per_seq);
+    tir_status rc = tokens_per_seq == 1 ? decode_forward(b) : forward(b, tokens_per_seq);
     if (rc != TIR_OK) return rc;
     if (next_ids_host) {
         e = cudaMemcpyAsync(b->h_next, b->next, static_cast<size_t>(b->B) * 4, cudaMemcpyDeviceToHost, b->stream);
@@ -550,28 +736,31 @@ tir_status tir_batch_generate(tir_batch* b, const int32_t* prompts_host, int32_t
         return fail(TIR_ERR_INVALID_ARG, "n_prompt must be in [1, " + std::to_string(b->max_tps) + "], cap >= 0");
     if (n_prompt + cap > b->max_ctx) return fail(TIR_ERR_CTX_OVERFLOW, "prompt + cap exceeds the batch context");
     cudaSetDevice(b->m->device);
-    b->len = 0;
+    tir_status rc = reset_len(b);
+    if (rc != TIR_OK) return rc;
     const size_t n = static_cast<size_t>(b->B) * n_prompt;
     cudaError_t e = cudaMemcpyAsync(b->ids, prompts_host, n * 4, cudaMemcpyHostToDevice, b->stream);
     if (e != cudaSuccess) return bfail(e, "prompt upload");
-    int32_t* gen = nullptr;  // [cap][B] on the device
-    if (cap > 0 && cudaMallocAsync(reinterpret_cast<void**>(&gen), static_cast<size_t>(cap) * b->B * 4, b->stream) !=
-                       cudaSuccess)
-        return fail(TIR_ERR_OOM, "output allocation failed");
-    tir_status rc = forward(b, n_prompt);
+    if (cap > b->gen_cap) {  // generated ids [cap][B] on the device
+        cudaStreamSynchronize(b->stream);
+        if (b->gen) cudaFree(b->gen);
+        b->gen = nullptr;
+        b->gen_cap = 0;
+        if (cudaMalloc(reinterpret_cast<void**>(&b->gen), static_cast<size_t>(cap) * b->B * 4) != cudaSuccess)
+            return fail(TIR_ERR_OOM, "output allocation failed");
+        b->gen_cap = cap;
+    }
+    rc = forward(b, n_prompt);
+    const unsigned fb = static_cast<unsigned>((b->B + 255) / 256);
     for (int i = 0; rc == TIR_OK && i < cap; ++i) {
-        // the sampled ids are both this step's output and its input
-        cudaMemcpyAsync(gen + static_cast<size_t>(i) * b->B, b->next, static_cast<size_t>(b->B) * 4,
-                        cudaMemcpyDeviceToDevice, b->stream);
-        cudaMemcpyAsync(b->ids, b->next, static_cast<size_t>(b->B) * 4, cudaMemcpyDeviceToDevice, b->stream);
-        rc = forward(b, 1);
+        feed_kernel<<<fb, 256, 0, b->stream>>>(b->next, b->ids, b->gen + static_cast<size_t>(i) * b->B, b->B);
+        rc = decode_forward(b);
     }
     std::vector<int32_t> host(static_cast<size_t>(cap) * b->B);
     if (rc == TIR_OK && cap > 0) {
-        e = cudaMemcpyAsync(host.data(), gen, host.size() * 4, cudaMemcpyDeviceToHost, b->stream);
+        e = cudaMemcpyAsync(host.data(), b->gen, host.size() * 4, cudaMemcpyDeviceToHost, b->stream);
         if (e != cudaSuccess) rc = bfail(e, "id readback");
     }
-    if (gen) cudaFreeAsync(gen, b->stream);
     const tir_status rc2 = check_err(b);
     if (rc == TIR_OK) rc = rc2;
     if (rc == TIR_OK)

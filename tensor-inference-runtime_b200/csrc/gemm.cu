@@ -15,18 +15,22 @@
 // Data flow per CTA (one 128-row weight tile x one NT-token tile, NT = 256,
 // or 64 for small batches; K in steps of 64): warp 0 streams each step's raw
 // Q8_0 block (8.5 KB) and the step's pre-split activation planes (NT x 256 B)
-// with TMA bulk copies into a 2- or 3-stage ring (each SM's copy engine spends
-// a fixed time per copy, so the copies are few and large); warps 2-5 expand the raw block into the 128B-swizzled f16 hi/lo A
-// planes; one thread of warp 1 issues the 12 tcgen05.mma of the step (4 K
-// sub-steps x 3 passes) and commits the stage back to the producer; after the
+// with TMA bulk copies into a ring of 2 (NT = 256) or 6 (NT = 64) stages
+// (each SM's copy engine spends a fixed time per copy, so the copies are few
+// and large); warps 2-5 expand each raw block into the 128B-swizzled f16
+// hi/lo A planes of a separate 2-stage ring, in packed f16 arithmetic (two
+// instructions per weight); one thread of warp 1 issues the 12 tcgen05.mma of
+// the step (4 K sub-steps x 3 passes) and commits both stages back; after the
 // last step warps 2-5 read the f32 accumulator out of TMEM.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <vector>
 
 #include "host.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "runtime.h"
 
@@ -40,23 +44,27 @@ constexpr int kGThreads = 192;
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
 constexpr int kGPlaneA = kGM * kGKS * 2;            // one f16 weight plane of a stage (16 KB)
 constexpr uint32_t kGErrTimeout = 25;
+constexpr int kGMaxSplits = 8;  // split-K CTAs of a tile: one cluster (portable size)
 
 template <int NT>
 struct GemmCfg {
-    static constexpr int kStages = NT >= 256 ? 2 : 3;
+    // TMA ring (raw weight block + activation planes of a K step): deep for
+    // small token tiles, whose steps are short, so that HBM latency is covered.
+    static constexpr int kRaw = NT >= 256 ? 2 : 6;
+    static constexpr int kConv = 2;                  // expanded weight-plane stages
     static constexpr int kPlaneX = NT * kGKS * 2;  // one f16 activation plane of a stage
 };
 
 template <int NT>
 struct GemmSmem {
-    static constexpr int S = GemmCfg<NT>::kStages;
-    uint8_t a[S][2 * kGPlaneA];                   // weight planes hi | lo (128B-swizzled, K-major)
-    uint8_t x[S][2 * GemmCfg<NT>::kPlaneX];       // activation planes hi | lo, as laid out in global
-    uint8_t w[S][kGWBytes];                       // raw Q8_0 block of the step (TMA target)
-    uint64_t full_raw[S], full_a[S], empty[S], acc;
+    using C = GemmCfg<NT>;
+    uint8_t a[C::kConv][2 * kGPlaneA];            // weight planes hi | lo (128B-swizzled, K-major)
+    uint8_t x[C::kRaw][2 * C::kPlaneX];           // activation planes hi | lo, as laid out in global
+    uint8_t w[C::kRaw][kGWBytes];                 // raw block of the step (TMA target)
+    uint64_t full_w[C::kRaw], full_x[C::kRaw], empty_raw[C::kRaw], full_a[C::kConv], empty_a[C::kConv], acc;
     uint32_t tmem_base;
     int32_t ok;
-    float inv_x[NT];
+    float inv_x[NT];  // 2^-kx of the tile's tokens
 };
 static_assert(offsetof(GemmSmem<256>, x) % 1024 == 0 && offsetof(GemmSmem<64>, x) % 1024 == 0,
               "swizzle atoms need 1 KB");
@@ -68,8 +76,8 @@ struct GemmParams {
     const float* w_pow2;     // [n rounded up to 128]: 2^kw of each row
     const uint8_t* xp;       // activation planes: [token tile][k step][hi | lo]
     const float* x_inv;      // [tokens rounded up to 128]: 2^-kx of each token
-    float* y;                // [splits][tokens][y_ld]
-    int32_t n, k, tokens, y_ld, ks_per_split;
+    float* y;                // [tokens][y_ld]: the product (or y + the product, accumulate != 0)
+    int32_t n, k, tokens, y_ld, ks_per_split, accumulate;
     uint32_t* err;
     unsigned long long timeout_ns;
 };
@@ -131,7 +139,8 @@ __device__ __forceinline__ bool gwait(const GemmParams& p, uint64_t* bar, uint32
 
 template <int NT>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_constant__ GemmParams p) {
-    constexpr int kGStages = GemmCfg<NT>::kStages;
+    constexpr int kRaw = GemmCfg<NT>::kRaw;
+    constexpr int kConv = GemmCfg<NT>::kConv;
     constexpr int kGPlaneX = GemmCfg<NT>::kPlaneX;
     extern __shared__ uint8_t g_smem_raw[];
     GemmSmem<NT>& s =
@@ -141,11 +150,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     const int nks_all = p.k / kGKS;
     const int ks0 = split * p.ks_per_split;
     const int nks = min(nks_all, ks0 + p.ks_per_split) - ks0;
+    const int splits = gridDim.z;  // launched as clusters of (1, 1, splits)
     if (tid == 0) {
-        for (int i = 0; i < kGStages; ++i) {
-            mbar_init(&s.full_raw[i], 1);
+        for (int i = 0; i < kRaw; ++i) {
+            mbar_init(&s.full_w[i], 1);
+            mbar_init(&s.full_x[i], 1);
+            mbar_init(&s.empty_raw[i], 4 + 1);  // the 4 converter warps + the MMAs' commit
+        }
+        for (int i = 0; i < kConv; ++i) {
             mbar_init(&s.full_a[i], 4);
-            mbar_init(&s.empty[i], 1);
+            mbar_init(&s.empty_a[i], 1);
         }
         mbar_init(&s.acc, 1);
         s.ok = 1;
@@ -156,42 +170,60 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                      "r"(static_cast<uint32_t>(NT)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    for (int i = tid; i < NT; i += kGThreads) s.inv_x[i] = p.x_inv[tt * NT + i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s.tmem_base;
+    if (tid == 0) griddep_launch_dependents();
 
     if (warp == 0) {
-        // ---- producer: raw weight block + activation planes of each K step
+        // ---- producer: raw weight block + activation planes of each K step.
+        // The weights do not depend on earlier work of the stream: the first
+        // stages' weight blocks are fetched before waiting for it.
         if (lane == 0) {
-            for (int i = 0; i < nks; ++i) {
-                const int st = i % kGStages;
-                if (i >= kGStages && !gwait(p, &s.empty[st], ((i / kGStages) - 1) & 1)) {
+            const uint8_t* wsrc = p.w + (static_cast<size_t>(rt) * nks_all + ks0) * kGWBytes;
+            const uint8_t* xsrc = p.xp + (static_cast<size_t>(tt) * nks_all + ks0) * (2 * kGPlaneX);
+            const int pre = min(nks, kRaw);
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&s.full_w[i], kGWBytes);
+                bulk_g2s(s.w[i], wsrc + static_cast<size_t>(i) * kGWBytes, kGWBytes, &s.full_w[i]);
+            }
+            griddep_wait();
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&s.full_x[i], 2 * kGPlaneX);
+                bulk_g2s(s.x[i], xsrc + static_cast<size_t>(i) * (2 * kGPlaneX), 2 * kGPlaneX, &s.full_x[i]);
+            }
+            int issued = pre;
+            for (int i = pre; i < nks; ++i) {
+                const int st = i % kRaw;
+                if (!gwait(p, &s.empty_raw[st], ((i / kRaw) - 1) & 1)) {
                     s.ok = 0;
                     break;
                 }
-                mbar_arrive_expect_tx(&s.full_raw[st], kGWBytes + 2 * kGPlaneX);
-                bulk_g2s(s.w[st], p.w + (static_cast<size_t>(rt) * nks_all + ks0 + i) * kGWBytes, kGWBytes,
-                         &s.full_raw[st]);
-                bulk_g2s(s.x[st], p.xp + (static_cast<size_t>(tt) * nks_all + ks0 + i) * (2 * kGPlaneX), 2 * kGPlaneX,
-                         &s.full_raw[st]);
+                mbar_arrive_expect_tx(&s.full_w[st], kGWBytes);
+                bulk_g2s(s.w[st], wsrc + static_cast<size_t>(i) * kGWBytes, kGWBytes, &s.full_w[st]);
+                mbar_arrive_expect_tx(&s.full_x[st], 2 * kGPlaneX);
+                bulk_g2s(s.x[st], xsrc + static_cast<size_t>(i) * (2 * kGPlaneX), 2 * kGPlaneX, &s.full_x[st]);
+                issued = i + 1;
             }
             // every copy issued lands before the CTA can leave
-            for (int i = max(0, nks - kGStages); i < nks; ++i) gwait(p, &s.full_raw[i % kGStages], (i / kGStages) & 1);
+            for (int i = max(0, issued - kRaw); i < issued; ++i) {
+                gwait(p, &s.full_w[i % kRaw], (i / kRaw) & 1);
+                gwait(p, &s.full_x[i % kRaw], (i / kRaw) & 1);
+            }
         }
     } else if (warp == 1) {
         // ---- MMA issue (one thread)
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>(kGM >> 4) << 24);
             for (int i = 0; i < nks; ++i) {
-                const int st = i % kGStages;
-                if (!gwait(p, &s.full_raw[st], (i / kGStages) & 1) || !gwait(p, &s.full_a[st], (i / kGStages) & 1)) {
+                const int st = i % kRaw, sa = i % kConv;
+                if (!gwait(p, &s.full_x[st], (i / kRaw) & 1) || !gwait(p, &s.full_a[sa], (i / kConv) & 1)) {
                     s.ok = 0;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_hi = smem_u32(s.a[st]), a_lo = a_hi + kGPlaneA;
+                const uint32_t a_hi = smem_u32(s.a[sa]), a_lo = a_hi + kGPlaneA;
                 const uint32_t x_hi = smem_u32(s.x[st]), x_lo = x_hi + kGPlaneX;
 #pragma unroll
                 for (int kk = 0; kk < kGKS / 16; ++kk) {
@@ -200,66 +232,143 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                     umma_f16(tmem, umma_desc(a_hi + o), umma_desc(x_lo + o), idesc, 1u);
                     umma_f16(tmem, umma_desc(a_lo + o), umma_desc(x_hi + o), idesc, 1u);
                 }
-                umma_commit(&s.empty[st]);  // the stage is free once these MMAs completed
+                // the weight planes and the activation planes are free once these MMAs completed
+                umma_commit(&s.empty_a[sa]);
+                umma_commit(&s.empty_raw[st]);
             }
             umma_commit(&s.acc);
         }
     } else {
-        // ---- converters: thread r expands weight row r of each step
+        // ---- converters: thread r expands weight row r of each step.  The raw
+        // block holds q + 128 as bytes and f16 scales already multiplied by
+        // the row's 2^kw, so a = q * s' (at most 19 significant bits, below
+        // 2^15) splits in packed f16 arithmetic: hi = RN(q * s'), and
+        // lo = q * s' - hi, exact in one fused multiply-add (at most 8
+        // significant bits, all at or above the last bit of s').  Bytes become
+        // f16 by the magic-number route: 0x64 << 8 | b is the f16 1024 + b.
         const int r = tid - 64;
-        const float pw = p.w_pow2[rt * kGM + r];
+        uint32_t offs[8];
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) offs[ch] = sw128_offset(r, ch * 8);
+        const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
         bool ok = true;
         for (int i = 0; i < nks && ok; ++i) {
-            const int st = i % kGStages;
-            ok = gwait(p, &s.full_raw[st], (i / kGStages) & 1);
+            const int st = i % kRaw, sa = i % kConv;
+            ok = gwait(p, &s.full_w[st], (i / kRaw) & 1);
+            if (ok && i >= kConv) ok = gwait(p, &s.empty_a[sa], ((i / kConv) - 1) & 1);
             if (ok) {
                 const uint8_t* wq = s.w[st] + r * kGKS;
-                const __half* ws = reinterpret_cast<const __half*>(s.w[st] + kGM * kGKS) + r * 2;
-                const float s0 = __half2float(ws[0]) * pw, s1 = __half2float(ws[1]) * pw;
-                uint8_t* ahi = s.a[st];
-                uint8_t* alo = s.a[st] + kGPlaneA;
+                const __half2 sc2 = reinterpret_cast<const __half2*>(s.w[st] + kGM * kGKS)[r];
+                const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
+                uint8_t* ahi = s.a[sa];
+                uint8_t* alo = s.a[sa] + kGPlaneA;
 #pragma unroll
                 for (int ch = 0; ch < 8; ++ch) {  // 8 columns per 16-byte chunk
                     const uint2 qv = *reinterpret_cast<const uint2*>(wq + ch * 8);
-                    const float sc = ch < 4 ? s0 : s1;
-                    __align__(16) __half hi[8];
-                    __align__(16) __half lo[8];
+                    const __half2 sc = ch < 4 ? s0 : s1;
+                    uint4 hv, lv;
+                    uint32_t* hp = &hv.x;
+                    uint32_t* lp = &lv.x;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const uint32_t word = e < 4 ? qv.x : qv.y;
-                        const float a = static_cast<float>(static_cast<int8_t>((word >> (8 * (e & 3))) & 0xffu)) * sc;
-                        hi[e] = __float2half_rn(a);
-                        lo[e] = __float2half_rn(a - __half2float(hi[e]));
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t word = e < 2 ? qv.x : qv.y;
+                        const uint32_t h = __byte_perm(word, 0x64646464u, (e & 1) ? 0x4342u : 0x4140u);
+                        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&h), bias);
+                        const __half2 hi = __hmul2(q, sc);
+                        const __half2 lo = __hfma2(q, sc, __hneg2(hi));
+                        hp[e] = *reinterpret_cast<const uint32_t*>(&hi);
+                        lp[e] = *reinterpret_cast<const uint32_t*>(&lo);
                     }
-                    const uint32_t off = sw128_offset(r, ch * 8);
-                    *reinterpret_cast<uint4*>(ahi + off) = *reinterpret_cast<const uint4*>(hi);
-                    *reinterpret_cast<uint4*>(alo + off) = *reinterpret_cast<const uint4*>(lo);
+                    *reinterpret_cast<uint4*>(ahi + offs[ch]) = hv;
+                    *reinterpret_cast<uint4*>(alo + offs[ch]) = lv;
                 }
                 fence_proxy_async_smem();  // generic-proxy writes, read by the tensor cores
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s.full_a[st]);
+            if (lane == 0) {
+                mbar_arrive(&s.full_a[sa]);
+                mbar_arrive(&s.empty_raw[st]);
+            }
         }
-        // ---- epilogue: TMEM lane quarter (warp % 4) holds weight rows 32 q .. 32 q + 31
+        // ---- epilogue: TMEM lane quarter (warp % 4) holds weight rows 32 q .. 32 q + 31;
+        // it reads 2^-kx per token and may add into y: after earlier work
+        griddep_wait();
+        for (int i = tid - 64; i < NT; i += 128) s.inv_x[i] = p.x_inv[tt * NT + i];
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
         const bool acc_ok = __all_sync(0xffffffffu, ok && gwait(p, &s.acc, 0));
         tc_fence_after();
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const int n = rt * kGM + row;
         const float inv_w = 1.0f / p.w_pow2[rt * kGM + row];
+        const float* inv_x = s.inv_x;
         if (acc_ok) {
+            // split-K: this CTA's partial tile goes to its own shared memory,
+            // token-major (the weight/activation rings are idle by now)
+            float* part = reinterpret_cast<float*>(s.a);
             for (int c0 = 0; c0 < NT; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
+                float yv[16];  // accumulate: every load of the group before its stores
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int t = tt * NT + c0 + j;
-                    if (t < p.tokens && n < p.n)
-                        p.y[(static_cast<size_t>(split) * p.tokens + t) * p.y_ld + n] =
-                            __uint_as_float(v[j]) * s.inv_x[c0 + j] * inv_w;
+                    yv[j] = splits == 1 && p.accumulate && t < p.tokens && n < p.n
+                                ? p.y[static_cast<size_t>(t) * p.y_ld + n]
+                                : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int t = tt * NT + c0 + j;
+                    const float val = __uint_as_float(v[j]) * inv_x[c0 + j] * inv_w;
+                    if (splits > 1) {
+                        part[(c0 + j) * kGM + row] = val;
+                    } else if (t < p.tokens && n < p.n) {
+                        p.y[static_cast<size_t>(t) * p.y_ld + n] = p.accumulate ? __fadd_rn(yv[j], val) : val;
+                    }
                 }
             }
         }
+    }
+    if (splits > 1) {
+        // Split-K over the cluster of the tile's `splits` CTAs: once every
+        // partial tile is in place, CTA j sums token slice j of the tile over
+        // the CTAs' shared memory in rank order (deterministic) and writes it.
+        cluster_sync();
+        if (warp >= 2) {
+            const int row = (warp & 3) * 32 + lane;
+            const int n = rt * kGM + row;
+            const int t_end = min(NT, p.tokens - tt * NT);
+            const int t0 = split * t_end / splits, t1 = (split + 1) * t_end / splits;
+            const uint32_t base = smem_u32(s.a) + static_cast<uint32_t>(row) * 4u;
+            constexpr int U = 8;  // tokens per round: U x splits loads in flight
+            for (int t = t0; t < t1; t += U) {
+                float v[U][kGMaxSplits], yv[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    yv[u] = 0.f;
+                    if (t + u < t1) {
+                        const uint32_t la = base + static_cast<uint32_t>((t + u) * kGM) * 4u;
+#pragma unroll
+                        for (int sp = 0; sp < kGMaxSplits; ++sp)
+                            if (sp < splits) v[u][sp] = ld_dsmem_f32(dsmem_map(la, sp));
+                        if (p.accumulate && n < p.n) yv[u] = p.y[static_cast<size_t>(tt * NT + t + u) * p.y_ld + n];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    if (t + u < t1 && n < p.n) {
+                        float acc = v[u][0];
+#pragma unroll
+                        for (int sp = 1; sp < kGMaxSplits; ++sp)
+                            if (sp < splits) acc = __fadd_rn(acc, v[u][sp]);
+                        p.y[static_cast<size_t>(tt * NT + t + u) * p.y_ld + n] =
+                            p.accumulate ? __fadd_rn(yv[u], acc) : acc;
+                    }
+                }
+            }
+        }
+        cluster_sync();  // no CTA leaves while a peer still reads its partial tile
     }
     tc_fence_before();
     __syncthreads();
@@ -269,10 +378,11 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
 
 // ---- layouts -----------------------------------------------------------------
 
-// Q8_0 blocks [n][k/32] -> [row tile][k step] blocks: 128 x 64 int8 quants
-// (row-major), then 128 x 2 f16 scales; rows past n stay zero.  Also 2^kw per
-// row: the power of two that brings 127 * (largest scale of the row) into
-// [2^14, 2^15).
+// Q8_0 blocks [n][k/32] -> [row tile][k step] blocks: 128 x 64 quants as
+// q + 128 bytes (row-major), then 128 x 2 f16 scales multiplied by the row's
+// 2^kw; rows past n stay zero.  2^kw, kept per row for the epilogue, brings
+// 127 * (largest scale of the row) into [2^14, 2^15), so every scaled scale
+// and every q * scale stays inside the f16 range.
 __global__ void gemm_repack_kernel(const uint8_t* __restrict__ blocks, int64_t n, int64_t k, uint8_t* __restrict__ out,
                                    float* __restrict__ pow2) {
     const int64_t nb = k / 32, nks = k / kGKS;
@@ -284,16 +394,6 @@ __global__ void gemm_repack_kernel(const uint8_t* __restrict__ blocks, int64_t n
         const uint8_t* src = blocks + (row * nb + b) * 34;
         const uint16_t sb = static_cast<uint16_t>(src[0] | (src[1] << 8));
         mx = fmaxf(mx, fabsf(__half2float(__ushort_as_half(sb))));
-        uint8_t* dst = out + (rtile * nks + b / 2) * kGWBytes;
-        uint4* q = reinterpret_cast<uint4*>(dst + r * kGKS + (b & 1) * 32);
-        uint32_t w[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            w[j] = static_cast<uint32_t>(src[2 + 4 * j]) | (static_cast<uint32_t>(src[3 + 4 * j]) << 8) |
-                   (static_cast<uint32_t>(src[4 + 4 * j]) << 16) | (static_cast<uint32_t>(src[5 + 4 * j]) << 24);
-        q[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        q[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        reinterpret_cast<uint16_t*>(dst + kGM * kGKS)[r * 2 + (b & 1)] = sb;
     }
     // 127 * mx < 2^E  ->  2^kw = 2^(15 - E); zero or non-finite rows: 1
     int e = 0;
@@ -303,25 +403,50 @@ __global__ void gemm_repack_kernel(const uint8_t* __restrict__ blocks, int64_t n
         frexpf(m, &e);  // m = f * 2^e, f in [0.5, 1): 2^(e-1) <= m < 2^e
         pw = ldexpf(1.0f, 15 - e);
     }
+    for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* src = blocks + (row * nb + b) * 34;
+        const uint16_t sb = static_cast<uint16_t>(src[0] | (src[1] << 8));
+        uint8_t* dst = out + (rtile * nks + b / 2) * kGWBytes;
+        uint4* q = reinterpret_cast<uint4*>(dst + r * kGKS + (b & 1) * 32);
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            w[j] = (static_cast<uint32_t>(src[2 + 4 * j]) | (static_cast<uint32_t>(src[3 + 4 * j]) << 8) |
+                    (static_cast<uint32_t>(src[4 + 4 * j]) << 16) | (static_cast<uint32_t>(src[5 + 4 * j]) << 24)) ^
+                   0x80808080u;
+        q[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        q[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        const __half sc = __float2half_rn(__half2float(__ushort_as_half(sb)) * pw);
+        reinterpret_cast<uint16_t*>(dst + kGM * kGKS)[r * 2 + (b & 1)] = __half_as_ushort(sc);
+    }
     pow2[row] = pw;
 }
 
-// Activations X [tokens][k] f32 -> [token tile][k step] planes (hi | lo,
-// 128B-swizzled, nt tokens x 64 columns each) and 2^-kx per token, one warp
-// per token (tile rows past `tokens` are zero).
-__global__ void gemm_x_planes_kernel(const float* __restrict__ x, int64_t tokens, int64_t k, int64_t tokens_pad,
-                                     int nt, uint8_t* __restrict__ planes, float* __restrict__ inv) {
-    const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (t >= tokens_pad) return;
-    const int64_t plane = static_cast<int64_t>(nt) * kGKS * 2;
-    const int64_t nks = k / kGKS, ttile = t / nt, tr = t % nt;
-    const float* row = x + t * k;
+// Activation rows -> [token tile][k step] planes (hi | lo, 128B-swizzled,
+// nt tokens x 64 columns each) and 2^-kx per token.  One CTA of kPlaneThreads
+// per token row (rows t >= tokens of the last tile are written as zeros);
+// val(c) gives column c of the row, evaluated once for the row's largest
+// magnitude and once for the split.
+constexpr int kPlaneThreads = 256;
+
+template <class F>
+__device__ __forceinline__ void planes_row(const F& val, bool live, int64_t t, int64_t k, int nt,
+                                           uint8_t* __restrict__ planes, float* __restrict__ inv) {
+    __shared__ float red[kPlaneThreads / 32];
+    const int tid = threadIdx.x;
+    const int64_t nch = k / 8;
     float mx = 0.f;
-    if (t < tokens)
-        for (int64_t c = lane; c < k; c += 32) mx = fmaxf(mx, fabsf(row[c]));
+    if (live)
+        for (int64_t ch = tid; ch < nch; ch += kPlaneThreads)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(val(ch * 8 + j)));
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < kPlaneThreads / 32; ++i) mx = fmaxf(mx, red[i]);
     int e = 0;
     float sx = 0.f, isx = 0.f;
     if (mx > 0.f && mx < 3.0e38f) {
@@ -329,33 +454,96 @@ __global__ void gemm_x_planes_kernel(const float* __restrict__ x, int64_t tokens
         sx = ldexpf(1.0f, 10 - e);
         isx = ldexpf(1.0f, e - 10);
     }
-    for (int64_t ch = lane; ch < k / 8; ch += 32) {  // 8-column chunks
-        const int64_t c0 = ch * 8, ks = c0 / kGKS, cc = c0 % kGKS;
-        __align__(16) __half hi[8];
-        __align__(16) __half lo[8];
+    const int64_t plane = static_cast<int64_t>(nt) * kGKS * 2;
+    const int64_t nks = k / kGKS, ttile = t / nt;
+    const int tr = static_cast<int>(t % nt);
+    for (int64_t ch = tid; ch < nch; ch += kPlaneThreads) {
+        const int64_t c0 = ch * 8, ks = c0 / kGKS;
+        const int cc = static_cast<int>(c0 % kGKS);
+        uint4 hv, lv;
+        uint32_t* hp = &hv.x;
+        uint32_t* lp = &lv.x;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const float v = t < tokens ? row[c0 + j] * sx : 0.f;
-            hi[j] = __float2half_rn(v);
-            lo[j] = __float2half_rn(v - __half2float(hi[j]));
+        for (int j = 0; j < 4; ++j) {
+            const float v0 = live ? val(c0 + 2 * j) * sx : 0.f;
+            const float v1 = live ? val(c0 + 2 * j + 1) * sx : 0.f;
+            const __half2 hi = __floats2half2_rn(v0, v1);
+            const float2 hf = __half22float2(hi);
+            const __half2 lo = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
+            hp[j] = *reinterpret_cast<const uint32_t*>(&hi);
+            lp[j] = *reinterpret_cast<const uint32_t*>(&lo);
         }
         uint8_t* base = planes + (ttile * nks + ks) * (2 * plane);
-        const uint32_t off = sw128_offset(static_cast<int>(tr), static_cast<int>(cc));
-        *reinterpret_cast<uint4*>(base + off) = *reinterpret_cast<const uint4*>(hi);
-        *reinterpret_cast<uint4*>(base + plane + off) = *reinterpret_cast<const uint4*>(lo);
+        const uint32_t off = sw128_offset(tr, cc);
+        *reinterpret_cast<uint4*>(base + off) = hv;
+        *reinterpret_cast<uint4*>(base + plane + off) = lv;
     }
-    if (lane == 0) inv[t] = isx;
+    if (tid == 0) inv[t] = isx;
 }
 
-// Sum of the split-K partial products, [splits][tokens][ld] -> [tokens][ld].
-__global__ void gemm_reduce_kernel(const float* __restrict__ part, int splits, int64_t tokens, int64_t n, int64_t ld,
-                                   float* __restrict__ y) {
-    const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (i >= tokens * n) return;
-    const int64_t t = i / n, c = i % n;
-    float acc = 0.f;
-    for (int sp = 0; sp < splits; ++sp) acc += part[(static_cast<int64_t>(sp) * tokens + t) * ld + c];
-    y[t * ld + c] = acc;
+// Planes of X [tokens][k] as given.
+__global__ void __launch_bounds__(kPlaneThreads) gemm_x_planes_kernel(const float* __restrict__ x, int64_t tokens,
+                                                                      int64_t k, int nt, uint8_t* __restrict__ planes,
+                                                                      float* __restrict__ inv) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int64_t t = blockIdx.x;
+    const float* row = x + t * k;
+    planes_row([&](int64_t c) { return row[c]; }, t < tokens, t, k, nt, planes, inv);
+}
+
+// Planes of rmsnorm(h) * w (src/math.rs:141-150, the division as a
+// multiplication by the correctly rounded reciprocal), h = row
+// rows ? rows[t] : t of X -- after X += Y on that row when Y is given (the
+// residual add of src/forward.rs, fused here so the matmul before it only
+// stores).
+__global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* __restrict__ X,
+                                                                         const float* __restrict__ Y,
+                                                                         const int32_t* __restrict__ rows,
+                                                                         int64_t tokens, int64_t k,
+                                                                         const float* __restrict__ w, float eps, int nt,
+                                                                         uint8_t* __restrict__ planes,
+                                                                         float* __restrict__ inv) {
+    __shared__ float part[kPlaneThreads / 32];
+    griddep_launch_dependents();
+    griddep_wait();
+    const int64_t t = blockIdx.x;
+    const bool live = t < tokens;
+    const int64_t xr = live ? (rows ? static_cast<int64_t>(rows[t]) : t) : 0;
+    float* x = X + xr * k;
+    if (live && Y) {
+        const float* y = Y + xr * k;
+        for (int64_t c = threadIdx.x; c < k; c += kPlaneThreads) x[c] = __fadd_rn(x[c], y[c]);
+        __syncthreads();
+    }
+    float ss = 0.f;
+    if (live)
+        for (int64_t c = threadIdx.x; c < k; c += kPlaneThreads) ss = fmaf(x[c], x[c], ss);
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.f;
+    for (int i = 0; i < kPlaneThreads / 32; ++i) total += part[i];
+    const float r = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(k)), eps)));
+    planes_row([&](int64_t c) { return __fmul_rn(__fmul_rn(x[c], w[c]), r); }, live, t, k, nt, planes, inv);
+}
+
+// Planes of h[t][j] = silu(gate) * up from interleaved (gate_j, up_j) columns
+// of GU [tokens][2 f] (src/math.rs:171-175).
+__global__ void __launch_bounds__(kPlaneThreads) gemm_silu_planes_kernel(const float* __restrict__ gu, int64_t tokens,
+                                                                         int64_t f, int nt,
+                                                                         uint8_t* __restrict__ planes,
+                                                                         float* __restrict__ inv) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int64_t t = blockIdx.x;
+    const float* row = gu + t * 2 * f;
+    planes_row(
+        [&](int64_t j) {
+            const float2 p = *reinterpret_cast<const float2*>(row + 2 * j);
+            return __fmul_rn(__fdiv_rn(p.x, __fadd_rn(1.0f, expf(-p.x))), p.y);
+        },
+        t < tokens, t, f, nt, planes, inv);
 }
 
 }  // namespace
@@ -382,7 +570,7 @@ int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out
     if (e != cudaSuccess) return static_cast<int>(e);
     const int64_t np = gemm_q8_rows_padded(n);
     if (np > n) {
-        // padded rows: scale 1 (their quants are zero)
+        // padded rows: 2^kw = 1 (their scales are zero)
         std::vector<float> ones(static_cast<size_t>(np - n), 1.0f);
         e = cudaMemcpyAsync(pow2 + n, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice, st);
         if (e != cudaSuccess) return static_cast<int>(e);
@@ -393,34 +581,125 @@ int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out
     return static_cast<int>(cudaGetLastError());
 }
 
-int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream) {
-    const int64_t tp = gemm_tokens_padded(tokens);
-    gemm_x_planes_kernel<<<static_cast<unsigned>((tp + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        x, tokens, k, tp, gemm_token_tile(tokens), planes, inv);
-    return static_cast<int>(cudaGetLastError());
+int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream,
+                         bool pdl) {
+    return static_cast<int>(launch_kernel(gemm_x_planes_kernel, dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))),
+                                          dim3(kPlaneThreads), 0, static_cast<cudaStream_t>(stream), pdl, x, tokens, k,
+                                          gemm_token_tile(tokens), planes, inv));
 }
 
-// y[t][n] (row stride y_ld) for t < tokens, n < n_rows; `part` (splits x
-// tokens x y_ld floats) is scratch for split-K, used when splits > 1.
-int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes, const float* x_inv, int64_t n,
-                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int splits, float* part, uint32_t* err,
-                   unsigned long long timeout_ns, void* stream) {
+int launch_gemm_norm_planes(float* X, const float* Y, const int32_t* rows, int64_t tokens, int64_t k, const float* w,
+                            float eps, uint8_t* planes, float* inv, void* stream, bool pdl) {
+    return static_cast<int>(launch_kernel(gemm_norm_planes_kernel,
+                                          dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))), dim3(kPlaneThreads),
+                                          0, static_cast<cudaStream_t>(stream), pdl, X, Y, rows, tokens, k, w, eps,
+                                          gemm_token_tile(tokens), planes, inv));
+}
+
+int launch_gemm_silu_planes(const float* gu, int64_t tokens, int64_t f, uint8_t* planes, float* inv, void* stream,
+                            bool pdl) {
+    return static_cast<int>(launch_kernel(gemm_silu_planes_kernel,
+                                          dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))), dim3(kPlaneThreads),
+                                          0, static_cast<cudaStream_t>(stream), pdl, gu, tokens, f,
+                                          gemm_token_tile(tokens), planes, inv));
+}
+
+int64_t gemm_tile_count(int64_t n, int64_t tokens) {
+    const int nt = gemm_token_tile(tokens);
+    return ((n + kGM - 1) / kGM) * ((tokens + nt - 1) / nt);
+}
+
+// Opt the matmul kernels into their shared memory on the current device
+// (once per thread and device; call it before capturing a launch in a graph).
+int gemm_configure() {
     static thread_local int configured = -1;
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured != dev) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(sizeof(GemmSmem<64>) + 1024));
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gemm_q8_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(sizeof(GemmSmem<256>) + 1024));
-        if (e != cudaSuccess) return static_cast<int>(e);
-        configured = dev;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    if (configured == dev) return 0;
+    e = cudaFuncSetAttribute(gemm_q8_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sizeof(GemmSmem<64>) + 1024));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_q8_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(sizeof(GemmSmem<256>) + 1024));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    configured = dev;
+    return 0;
+}
+
+namespace {
+
+// Clusters of `size` matmul CTAs (token tile nt) that can be resident at once
+// on the current device (cached; 0 when the query fails).
+int max_active_clusters(int nt, int size) {
+    static thread_local int dev_cached = -1;
+    static thread_local int cache[2][kGMaxSplits + 1];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (dev != dev_cached) {
+        for (auto& r : cache)
+            for (int& v : r) v = -1;
+        dev_cached = dev;
     }
+    int& c = cache[nt == 64 ? 0 : 1][size];
+    if (c >= 0) return c;
+    if (gemm_configure() != 0) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, static_cast<unsigned>(size));
+    cfg.blockDim = dim3(kGThreads);
+    cfg.dynamicSmemBytes = (nt == 64 ? sizeof(GemmSmem<64>) : sizeof(GemmSmem<256>)) + 1024;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 1;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = static_cast<unsigned>(size);
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const cudaError_t e = nt == 64 ? cudaOccupancyMaxActiveClusters(&n, gemm_q8_kernel<64>, &cfg)
+                                   : cudaOccupancyMaxActiveClusters(&n, gemm_q8_kernel<256>, &cfg);
+    c = e == cudaSuccess ? n : 0;
+    return c;
+}
+
+}  // namespace
+
+// Split-K factor for a matmul on `sms` multiprocessors (one CTA each): none
+// when the tiles alone fill the GPU, else the fewest waves of the shortest
+// CTAs, a wave being as many clusters of that size as fit at once, each CTA
+// paying about three K steps of pipeline fill.
+int gemm_splits(int64_t n, int64_t k, int64_t tokens, int sms) {
+    const int64_t tiles = gemm_tile_count(n, tokens), nks = k / kGKS;
+    if (tiles <= 0 || nks <= 0 || sms <= 0 || tiles >= sms) return 1;
+    const int nt = gemm_token_tile(tokens);
+    int best = 1;
+    int64_t best_cost = (tiles + sms - 1) / sms * (nks + 3);
+    for (int64_t sp = 2; sp <= std::min<int64_t>(nks, kGMaxSplits); ++sp) {
+        const int64_t per = (nks + sp - 1) / sp, real = (nks + per - 1) / per;
+        if (real != sp) continue;
+        const int cap = max_active_clusters(nt, static_cast<int>(sp));
+        if (cap <= 0) continue;
+        const int64_t cost = (tiles + cap - 1) / cap * (per + 3);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = static_cast<int>(sp);
+        }
+    }
+    return best;
+}
+
+// y[t][n] (row stride y_ld) for t < tokens, n < n_rows, or y += that when
+// accumulate != 0.  splits > 1 (at most kGMaxSplits) divides K over that many
+// CTAs per tile, launched as one thread-block cluster that sums its partial
+// tiles in distributed shared memory.
+int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes, const float* x_inv, int64_t n,
+                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int accumulate, int splits, uint32_t* err,
+                   unsigned long long timeout_ns, void* stream, bool pdl) {
+    const int cfg = gemm_configure();
+    if (cfg != 0) return cfg;
     const int nt = gemm_token_tile(tokens);
     const int nks = static_cast<int>(k / kGKS);
-    if (splits < 1) splits = 1;
-    if (splits > nks) splits = nks;
+    splits = std::max(1, std::min({splits, nks, kGMaxSplits}));
     GemmParams p{};
     p.w = w;
     p.w_pow2 = w_pow2;
@@ -430,23 +709,21 @@ int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes,
     p.k = static_cast<int32_t>(k);
     p.tokens = static_cast<int32_t>(tokens);
     p.y_ld = static_cast<int32_t>(y_ld);
+    p.accumulate = accumulate ? 1 : 0;
     p.ks_per_split = (nks + splits - 1) / splits;
     splits = (nks + p.ks_per_split - 1) / p.ks_per_split;
-    p.y = splits > 1 ? part : y;
+    p.y = y;
     p.err = err;
     p.timeout_ns = timeout_ns;
     const dim3 grid(static_cast<unsigned>((n + kGM - 1) / kGM), static_cast<unsigned>((tokens + nt - 1) / nt),
                     static_cast<unsigned>(splits));
+    const dim3 cluster(1, 1, static_cast<unsigned>(splits));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (nt == 64)
-        gemm_q8_kernel<64><<<grid, kGThreads, sizeof(GemmSmem<64>) + 1024, st>>>(p);
-    else
-        gemm_q8_kernel<256><<<grid, kGThreads, sizeof(GemmSmem<256>) + 1024, st>>>(p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess || splits == 1) return static_cast<int>(e);
-    const int64_t total = tokens * n;
-    gemm_reduce_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(part, splits, tokens, n, y_ld, y);
-    return static_cast<int>(cudaGetLastError());
+    const cudaError_t e = nt == 64 ? launch_kernel_cluster(gemm_q8_kernel<64>, grid, dim3(kGThreads),
+                                                            sizeof(GemmSmem<64>) + 1024, st, pdl, cluster, p)
+                                   : launch_kernel_cluster(gemm_q8_kernel<256>, grid, dim3(kGThreads),
+                                                           sizeof(GemmSmem<256>) + 1024, st, pdl, cluster, p);
+    return static_cast<int>(e);
 }
 
 }  // namespace tir

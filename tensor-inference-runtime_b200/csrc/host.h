@@ -123,10 +123,27 @@ int64_t gemm_q8_rows_padded(int64_t n);
 int64_t gemm_x_plane_bytes(int64_t tokens, int64_t k);
 int64_t gemm_tokens_padded(int64_t tokens);
 int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out, float* pow2, void* stream);
-int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream);
+// pdl: launched with a programmatic dependency on the stream's previous work.
+int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream,
+                         bool pdl = false);
+// Planes of rmsnorm(X[r]) * w, r = rows ? rows[t] : t for t < tokens, after
+// X[r] += Y[r] when Y is not null.
+int launch_gemm_norm_planes(float* X, const float* Y, const int32_t* rows, int64_t tokens, int64_t k, const float* w,
+                            float eps, uint8_t* planes, float* inv, void* stream, bool pdl = false);
+// Planes of silu(gate) * up from interleaved (gate, up) columns of gu [tokens][2 f].
+int launch_gemm_silu_planes(const float* gu, int64_t tokens, int64_t f, uint8_t* planes, float* inv, void* stream,
+                            bool pdl = false);
+// Shared-memory opt-in of the matmul kernels on the current device (0 or a cudaError_t).
+int gemm_configure();
+// Weight-row tiles x token tiles of a matmul of n rows over `tokens` rows.
+int64_t gemm_tile_count(int64_t n, int64_t tokens);
+// Split-K factor for a matmul on `sms` multiprocessors.
+int gemm_splits(int64_t n, int64_t k, int64_t tokens, int sms);
+// y (row stride y_ld) = the matmul of the planes with the prepared weights,
+// or y += it (accumulate); split-K over `splits` CTAs per tile (one cluster).
 int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes, const float* x_inv, int64_t n,
-                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int splits, float* part, uint32_t* err,
-                   unsigned long long timeout_ns, void* stream);
+                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int accumulate, int splits, uint32_t* err,
+                   unsigned long long timeout_ns, void* stream, bool pdl = false);
 
 // Rows per weight tile of a matrix with k columns (0: unsupported k).
 int tile_rows_for(int64_t k, bool pairs);

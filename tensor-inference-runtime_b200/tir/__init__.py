@@ -137,9 +137,6 @@ SIGNATURES = {
 }
 
 _lib = None
-_FINALIZERS = {}
-
-
 def lib():
     """Loads libtir.so (built in-tree by tir.build); raises if it is absent."""
     global _lib
@@ -152,8 +149,6 @@ def lib():
             fn = getattr(L, name)
             fn.restype = res
             fn.argtypes = args
-        for name in ("tir_gguf_close", "tir_model_destroy", "tir_state_destroy", "tir_batch_destroy"):
-            _FINALIZERS[name] = getattr(L, name)
         _lib = L
     return _lib
 
@@ -196,6 +191,7 @@ class GGUF:
 
     def __init__(self, handle):
         self._h = C.c_void_p(handle)
+        self._destroy = lib().tir_gguf_close  # held by the object: usable at interpreter teardown
 
     @classmethod
     def open(cls, path):
@@ -225,10 +221,10 @@ class GGUF:
             g.close()
 
     def close(self):
-        if getattr(self, "_h", None):
-            # bound at import time: finalizers may run after module teardown
-            _FINALIZERS["tir_gguf_close"](self._h)
+        h = getattr(self, "_h", None)
+        if h:
             self._h = None
+            self._destroy(h)
 
     def __del__(self):
         self.close()
@@ -311,6 +307,7 @@ class Model:
         else:
             check(lib().tir_model_load(os.fsencode(path), device, C.byref(h)))
         self._h = h
+        self._destroy = lib().tir_model_destroy  # held by the object: usable at interpreter teardown
         self.device = device
         t = Transformer()
         check(lib().tir_model_info(self._h, C.byref(t)))
@@ -327,10 +324,10 @@ class Model:
         check(lib().tir_model_set_mode(self._h, mode))
 
     def close(self):
-        if getattr(self, "_h", None):
-            # bound at import time: finalizers may run after module teardown
-            _FINALIZERS["tir_model_destroy"](self._h)
+        h = getattr(self, "_h", None)
+        if h:
             self._h = None
+            self._destroy(h)
 
     def __del__(self):
         self.close()
@@ -347,6 +344,7 @@ class State:
         h = C.c_void_p()
         check(lib().tir_state_create(model.handle, max_ctx, C.byref(h)))
         self._h = h
+        self._destroy = lib().tir_state_destroy  # held by the object: usable at interpreter teardown
         self.max_ctx = max_ctx
         self.vocab = model.info["vocab"]
         self.embed_dim = model.info["embed_dim"]
@@ -357,10 +355,10 @@ class State:
         return self._h
 
     def close(self):
-        if getattr(self, "_h", None):
-            # bound at import time: finalizers may run after module teardown
-            _FINALIZERS["tir_state_destroy"](self._h)
+        h = getattr(self, "_h", None)
+        if h:
             self._h = None
+            self._destroy(h)
 
     def __del__(self):
         self.close()
@@ -456,16 +454,17 @@ class Batch:
         h = C.c_void_p()
         check(lib().tir_batch_create(model.handle, n_seqs, max_ctx, max_tokens_per_seq, C.byref(h)))
         self._h = h
+        self._destroy = lib().tir_batch_destroy  # held by the object: usable at interpreter teardown
 
     @property
     def handle(self):
         return self._h
 
     def close(self):
-        if getattr(self, "_h", None):
-            # bound at import time: finalizers may run after module teardown
-            _FINALIZERS["tir_batch_destroy"](self._h)
+        h = getattr(self, "_h", None)
+        if h:
             self._h = None
+            self._destroy(h)
 
     def __del__(self):
         self.close()

@@ -59,4 +59,9 @@ def test_batch_errors(tirlib, tiny):
         b.step(np.array([[1], [m.info["vocab"]]], np.int32))
     assert e.value.name == "BAD_TOKEN"
     assert len(b) == 0
+    # the error is cleared with the reset: the batch decodes again
+    nxt = b.step(np.array([[1], [2]], np.int32))
+    assert nxt.shape == (2,) and len(b) == 1
+    nxt = b.step(nxt[:, None])
+    assert len(b) == 2
     b.close()

@@ -334,7 +334,7 @@ def test_swiglu(cuda, tirlib, orc):
 
 
 @pytest.mark.parametrize("tokens,k,n", [(64, 2048, 2560), (300, 2048, 2048), (128, 5632, 2048), (7, 128, 7),
-                                        (1, 2048, 32000), (257, 1024, 130)])
+                                        (1, 2048, 32000), (257, 1024, 130), (64, 2048, 11264), (33, 5632, 2048)])
 def test_q8_matmul_batch_vs_oracle(cuda, tirlib, orc, tokens, k, n):
     """Tensor-core batched matmul (3-pass f16 split, f32 accumulation) against
     the oracle's q8_matmul token by token: rel-L2 below 1e-5 per token."""
