@@ -1030,15 +1030,18 @@ tir_status tir_q8_matmul_batch(const float* x, int64_t tokens, const uint8_t* w,
     if (!c) return fail(TIR_ERR_OOM, "device context allocation failed");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int sms = decode_grid_size(dev);
-    const int splits = gemm_splits(n, k, tokens, sms);
+    const int splits = gemm_real_splits(k, gemm_splits(n, k, tokens, sms));
     uint8_t* planes = nullptr;
     const size_t pbytes = static_cast<size_t>(gemm_x_plane_bytes(tokens, k));
     const size_t ibytes = static_cast<size_t>(gemm_tokens_padded(tokens)) * 4;
-    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&planes), pbytes + ibytes, st), "batched matmul scratch");
+    const size_t sbytes = splits > 1 ? static_cast<size_t>(splits) * tokens * n * 4 : 0;
+    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&planes), pbytes + ibytes + sbytes, st),
+             "batched matmul scratch");
     float* inv = reinterpret_cast<float*>(planes + pbytes);
+    float* part = splits > 1 ? reinterpret_cast<float*>(planes + pbytes + ibytes) : y;
     int rc = launch_gemm_x_planes(x, tokens, k, planes, inv, stream);
-    if (rc == 0)
-        rc = launch_gemm_q8(w, w_pow2, planes, inv, n, k, tokens, y, n, 0, splits, c->error, timeout_ns(), stream);
+    if (rc == 0) rc = launch_gemm_q8(w, w_pow2, planes, inv, n, k, tokens, part, n, splits, c->error, timeout_ns(), stream);
+    if (rc == 0 && splits > 1) rc = launch_gemm_sum_parts(part, splits, tokens * n, tokens * n, y, stream);
     cudaFreeAsync(planes, st);
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "batched q8 matmul");
     return TIR_OK;

@@ -15,6 +15,7 @@
 
 #include "host.h"
 #include "launch.cuh"
+#include "parts.cuh"
 #include "ptx.cuh"
 #include "runtime.h"
 
@@ -68,25 +69,28 @@ __global__ void embed_rows_kernel(const int32_t* __restrict__ ids, const uint8_t
 // RoPE on the q and k parts of each token's fused q|k|v row (src/math.rs:196-228),
 // then the KV-cache append (src/forward.rs:83-84).  Token t belongs to
 // sequence t / tps at position *pos0 + t % tps; cache [seq][max_ctx][kvd].
-__global__ void rope_append_kernel(float* __restrict__ qkv, int64_t ld, int tps, const int32_t* pos0, int H, int kvd,
-                                   int max_ctx, const float* __restrict__ rc, const float* __restrict__ rs,
-                                   float* __restrict__ kc, float* __restrict__ vc) {
+__global__ void rope_append_kernel(float* __restrict__ qkv, int parts, int64_t part, int64_t ld, int tps,
+                                   const int32_t* pos0, int H, int kvd, int max_ctx, const float* __restrict__ rc,
+                                   const float* __restrict__ rs, float* __restrict__ kc, float* __restrict__ vc) {
     griddep_launch_dependents();
     griddep_wait();
     const int64_t t = blockIdx.x;
     const int64_t s = t / tps;
     const int pos = *pos0 + static_cast<int>(t % tps);
     float* row = qkv + t * ld;
+    // the q|k|v row: the sum of the matmul's partial tiles (into tile 0)
+    sum_parts_inplace(row, parts, part, H + 2 * kvd);
+    auto val = [&](int c) { return row[c]; };
     const size_t cache_row = (static_cast<size_t>(s) * max_ctx + pos) * kvd;
     for (int pr = threadIdx.x; pr < (H + kvd) / 2; pr += blockDim.x) {
         const int c = 2 * pr;
         const int i = (c % kHeadDim) >> 1;
         const float cs = rc[static_cast<size_t>(pos) * (kHeadDim / 2) + i];
         const float sn = rs[static_cast<size_t>(pos) * (kHeadDim / 2) + i];
-        const float y0 = row[c], y1 = row[c + 1];
+        const float y0 = val(c), y1 = val(c + 1);
         const float e0 = __fadd_rn(__fmul_rn(cs, y0), __fmul_rn(-sn, y1));
         const float e1 = __fadd_rn(__fmul_rn(sn, y0), __fmul_rn(cs, y1));
-        if (c < H) {
+        if (c < H) {  // the attention kernels read q (roped) from partial tile 0
             row[c] = e0;
             row[c + 1] = e1;
         } else {
@@ -94,7 +98,7 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int64_t ld, int tps,
             kc[cache_row + (c - H) + 1] = e1;
         }
     }
-    for (int c = threadIdx.x; c < kvd; c += blockDim.x) vc[cache_row + c] = row[H + kvd + c];
+    for (int c = threadIdx.x; c < kvd; c += blockDim.x) vc[cache_row + c] = val(H + kvd + c);
 }
 
 // Causal grouped-query attention for tps >= 2 new tokens per sequence
@@ -227,20 +231,27 @@ __global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const flo
 }
 
 // One new token per sequence (decode), src/forward.rs:79-174: CTA per
-// (sequence, kv head) with kAttnWarps warps splitting the key positions in
-// chunks of 32 (warp w takes chunks w, w + kAttnWarps, ...).  Lane j scores
-// key j of its chunk against every query head of the group (queries in
-// shared memory), the warp folds the chunk into a running (max, sum, output)
-// per head with lanes over output dimensions, and the warps' states merge at
-// the end.  Scale 1/sqrt(64), softmax with the running-max shift.
+// (sequence, kv head).  First the CTA finishes the q|k|v projection for its
+// kv head (the sum of the matmul's `parts` partial tiles), applies RoPE to its
+// query heads and key (src/math.rs:196-228) and appends key and value to the
+// cache (src/forward.rs:83-84).  Then kAttnWarps warps split the key
+// positions in chunks of 32 (warp w takes chunks w, w + kAttnWarps, ...):
+// lane j scores key j of its chunk against every query head of the group
+// (queries in shared memory), the warp folds the chunk into a running (max,
+// sum, output) per head with lanes over output dimensions, and the warps'
+// states merge at the end.  Scale 1/sqrt(64), softmax with the running-max
+// shift.
 constexpr int kAttnWarps = 8;
+constexpr int kMaxParts = 16;  // split-K partial tiles a reader sums
 
 template <int G>  // query heads per kv head, rounded up (heads >= group are computed on zeros, not stored)
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const float* __restrict__ qkv, int64_t ld,
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const float* __restrict__ qkv, int parts,
+                                                                      int64_t part, int64_t ld,
                                                                       const int32_t* posp, int H, int kvd, int group,
-                                                                      int max_ctx,
-                                                                      const float* __restrict__ kc,
-                                                                      const float* __restrict__ vc,
+                                                                      int max_ctx, const float* __restrict__ rc,
+                                                                      const float* __restrict__ rs,
+                                                                      float* __restrict__ kc,
+                                                                      float* __restrict__ vc,
                                                                       float* __restrict__ out) {
     griddep_launch_dependents();
     griddep_wait();
@@ -249,10 +260,39 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
     __shared__ float os[kAttnWarps][G][kHeadDim];
     const int s = blockIdx.x, g = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int e = threadIdx.x; e < G * kHeadDim; e += blockDim.x)
-        qs[e / kHeadDim][e % kHeadDim] =
-            e / kHeadDim < group ? qkv[static_cast<int64_t>(s) * ld + (g * group) * kHeadDim + e] : 0.f;
-    __syncthreads();
+    const int pos = *posp;
+    const float* row = qkv + static_cast<int64_t>(s) * ld;
+    auto val = [&](int c) {  // partial loads first, then the sum in partial order
+        float v[kMaxParts];
+#pragma unroll
+        for (int j = 0; j < kMaxParts; ++j) v[j] = j < parts ? row[j * part + c] : 0.f;
+        float acc = v[0];
+#pragma unroll
+        for (int j = 1; j < kMaxParts; ++j)
+            if (j < parts) acc = __fadd_rn(acc, v[j]);
+        return acc;
+    };
+    const size_t cache_row = (static_cast<size_t>(s) * max_ctx + pos) * kvd + static_cast<size_t>(g) * kHeadDim;
+    for (int pr = threadIdx.x; pr < (group + 1) * (kHeadDim / 2); pr += blockDim.x) {
+        const bool isq = pr < group * (kHeadDim / 2);
+        const int i = pr % (kHeadDim / 2);  // rotation pair within the head
+        const int c = isq ? (g * group) * kHeadDim + 2 * pr : H + g * kHeadDim + 2 * i;
+        const float cs = rc[static_cast<size_t>(pos) * (kHeadDim / 2) + i];
+        const float sn = rs[static_cast<size_t>(pos) * (kHeadDim / 2) + i];
+        const float y0 = val(c), y1 = val(c + 1);
+        const float e0 = __fadd_rn(__fmul_rn(cs, y0), __fmul_rn(-sn, y1));
+        const float e1 = __fadd_rn(__fmul_rn(sn, y0), __fmul_rn(cs, y1));
+        if (isq) {
+            qs[pr / (kHeadDim / 2)][2 * i] = e0;
+            qs[pr / (kHeadDim / 2)][2 * i + 1] = e1;
+        } else {
+            kc[cache_row + 2 * i] = e0;
+            kc[cache_row + 2 * i + 1] = e1;
+        }
+    }
+    for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) vc[cache_row + d] = val(H + kvd + g * kHeadDim + d);
+    for (int e = group * kHeadDim + threadIdx.x; e < G * kHeadDim; e += blockDim.x) qs[e / kHeadDim][e % kHeadDim] = 0.f;
+    __syncthreads();  // queries staged; the new key and value visible to the CTA
     float m[G], l[G], o0[G], o1[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
@@ -261,7 +301,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
         o0[h] = 0.f;
         o1[h] = 0.f;
     }
-    const int n = *posp + 1;
+    const int n = pos + 1;
     const float* kb = kc + static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
     const float* vb = vc + static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
     for (int c0 = warp * 32; c0 < n; c0 += kAttnWarps * 32) {
@@ -340,15 +380,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
     }
 }
 
-// Greedy sample per row (src/tokenizer.rs:152-167: total order, ties -> last).
-__global__ void argmax_rows_kernel(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out) {
+// Greedy sample per row (src/tokenizer.rs:152-167: total order, ties -> last)
+// of logits that are the sum of `parts` partial tiles `part` floats apart.
+__global__ void argmax_rows_kernel(const float* __restrict__ x, int parts, int64_t part, int64_t n,
+                                   int32_t* __restrict__ out) {
     griddep_launch_dependents();
     griddep_wait();
     __shared__ unsigned long long red[32];
     const float* r = x + static_cast<int64_t>(blockIdx.x) * n;
     unsigned long long best = 0ull;
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const uint32_t b = __float_as_uint(r[i]);
+        float v = r[i];
+        for (int j = 1; j < parts; ++j) v = __fadd_rn(v, r[j * part + i]);
+        const uint32_t b = __float_as_uint(v);
         const uint32_t key = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
         best = max(best, (static_cast<unsigned long long>(key) << 32) | static_cast<uint32_t>(i));
     }
@@ -456,13 +500,16 @@ tir_status make_gw(tir_batch* b, const Mat& mt, uint8_t* staging, tir_batch::GW&
     return TIR_OK;
 }
 
-// y (row stride g.n) = the matmul of the activation planes in b->planes (as
-// written for `tokens` rows) with g, or y += it when accumulate.
-tir_status mm(tir_batch* b, int64_t tokens, const tir_batch::GW& g, float* y, bool accumulate) {
-    const int splits = gemm_splits(g.n, g.k, tokens, b->sms);
-    const int rc = launch_gemm_q8(g.w, g.p2, b->planes, b->inv, g.n, g.k, tokens, y, g.n, accumulate ? 1 : 0, splits,
-                                  b->err, 2000ull * 1000000ull, b->stream, true);
+// The matmul of the activation planes in b->planes (as written for `tokens`
+// rows) with g: *parts partial tiles of tokens x g.n floats from y on, whose
+// sum in order is the product.
+tir_status mm(tir_batch* b, int64_t tokens, const tir_batch::GW& g, float* y, int* parts) {
+    const int splits = gemm_real_splits(g.k, gemm_splits(g.n, g.k, tokens, b->sms));
+    if (splits > kMaxParts) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "more split-K partial tiles than a reader sums");
+    const int rc = launch_gemm_q8(g.w, g.p2, b->planes, b->inv, g.n, g.k, tokens, y, g.n, splits, b->err,
+                                  2000ull * 1000000ull, b->stream, true);
     if (rc != 0) return bfail(static_cast<cudaError_t>(rc), "tensor-core matmul");
+    *parts = splits;
     return TIR_OK;
 }
 
@@ -470,14 +517,15 @@ tir_status planes_rc(int rc) {
     return rc == 0 ? TIR_OK : bfail(static_cast<cudaError_t>(rc), "activation planes");
 }
 
-// Decode attention over the group size rounded up to an instantiated width.
-void attn_decode(tir_batch* b, int group, int kv_heads, int H, int KVD, int64_t ldq, const float* kc,
-                 const float* vc) {
+// Decode attention (with the q|k|v partial sum, RoPE and KV append) over the
+// group size rounded up to an instantiated width.
+void attn_decode(tir_batch* b, int parts, int group, int kv_heads, int H, int KVD, int64_t ldq, float* kc, float* vc) {
     const dim3 grid(static_cast<unsigned>(b->B), static_cast<unsigned>(kv_heads));
     const unsigned th = kAttnWarps * 32;
-#define TIR_ATTN(GM) \
-    launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, ldq, b->len_dev, H, KVD, group, \
-                  b->max_ctx, kc, vc, b->ATT)
+    const int64_t part = static_cast<int64_t>(b->B) * ldq;
+#define TIR_ATTN(GM)                                                                                                 \
+    launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, parts, part, ldq, b->len_dev, H, \
+                  KVD, group, b->max_ctx, b->rcos, b->rsin, kc, vc, b->ATT)
     if (group <= 1)
         TIR_ATTN(1);
     else if (group <= 2)
@@ -510,19 +558,20 @@ tir_status forward(tir_batch* b, int tps) {
     tir_status rc;
     launch_kernel(embed_rows_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->ids, m->embd.q,
                   m->embd.s, m->embd.sk, H, V, b->X, b->err);
+    int parts = 0, y_parts = 0;  // partial tiles of the latest matmul / of the one in Y
     for (int l = 0; l < L; ++l) {
         // the residual add of the previous layer's down projection (none before layer 0)
-        if ((rc = planes_rc(launch_gemm_norm_planes(b->X, l > 0 ? b->Y : nullptr, nullptr, T, H, m->attn_norm[l],
-                                                    1e-5f, b->planes, b->inv, st, true))) != TIR_OK)
+        if ((rc = planes_rc(launch_gemm_norm_planes(b->X, l > 0 ? b->Y : nullptr, y_parts, T * H, nullptr, T, H,
+                                                    m->attn_norm[l], 1e-5f, b->planes, b->inv, st, true))) != TIR_OK)
             return rc;
-        if ((rc = mm(b, T, b->qkv[l], b->QKV, false)) != TIR_OK) return rc;
+        if ((rc = mm(b, T, b->qkv[l], b->QKV, &parts)) != TIR_OK) return rc;
         float* kc = b->kc + l * layer_cache;
         float* vc = b->vc + l * layer_cache;
-        launch_kernel(rope_append_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->QKV, ldq, tps,
-                      b->len_dev, H, KVD, b->max_ctx, b->rcos, b->rsin, kc, vc);
         if (tps == 1) {
-            attn_decode(b, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);
+            attn_decode(b, parts, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);
         } else {
+            launch_kernel(rope_append_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->QKV, parts,
+                          T * ldq, ldq, tps, b->len_dev, H, KVD, b->max_ctx, b->rcos, b->rsin, kc, vc);
             launch_kernel(attn_prefill_kernel,
                           dim3(b->B, static_cast<unsigned>(t.k_v_heads * ((group + kPHeads - 1) / kPHeads)),
                                (tps + kQBlock - 1) / kQBlock),
@@ -530,22 +579,24 @@ tir_status forward(tir_batch* b, int tps) {
                           vc, b->ATT);
         }
         if ((rc = planes_rc(launch_gemm_x_planes(b->ATT, T, H, b->planes, b->inv, st, true))) != TIR_OK) return rc;
-        if ((rc = mm(b, T, b->o[l], b->Y, false)) != TIR_OK) return rc;
-        if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, nullptr, T, H, m->ffn_norm[l], 1e-5f, b->planes,
-                                                    b->inv, st, true))) != TIR_OK)
+        if ((rc = mm(b, T, b->o[l], b->Y, &y_parts)) != TIR_OK) return rc;
+        if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, y_parts, T * H, nullptr, T, H, m->ffn_norm[l], 1e-5f,
+                                                    b->planes, b->inv, st, true))) != TIR_OK)
             return rc;
-        if ((rc = mm(b, T, b->gu[l], b->GU, false)) != TIR_OK) return rc;
-        if ((rc = planes_rc(launch_gemm_silu_planes(b->GU, T, F, b->planes, b->inv, st, true))) != TIR_OK) return rc;
-        if ((rc = mm(b, T, b->down[l], b->Y, false)) != TIR_OK) return rc;
+        if ((rc = mm(b, T, b->gu[l], b->GU, &parts)) != TIR_OK) return rc;
+        if ((rc = planes_rc(launch_gemm_silu_planes(b->GU, parts, T * 2 * F, T, F, b->planes, b->inv, st, true))) !=
+            TIR_OK)
+            return rc;
+        if ((rc = mm(b, T, b->down[l], b->Y, &y_parts)) != TIR_OK) return rc;
     }
     launch_kernel(last_rows_kernel, dim3((b->B + 127) / 128), dim3(128), 0, st, true, b->rows, b->B, tps, b->len_dev);
     // the last down projection's residual add, on the rows the logits need
-    if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, b->rows, b->B, H, m->out_norm, 1e-5f, b->planes, b->inv,
-                                                st, true))) != TIR_OK)
+    if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, y_parts, T * H, b->rows, b->B, H, m->out_norm, 1e-5f,
+                                                b->planes, b->inv, st, true))) != TIR_OK)
         return rc;
-    if ((rc = mm(b, b->B, b->lm, b->LG, false)) != TIR_OK) return rc;
-    launch_kernel(argmax_rows_kernel, dim3(static_cast<unsigned>(b->B)), dim3(256), 0, st, true, b->LG,
-                  static_cast<int64_t>(V), b->next);
+    if ((rc = mm(b, b->B, b->lm, b->LG, &parts)) != TIR_OK) return rc;
+    launch_kernel(argmax_rows_kernel, dim3(static_cast<unsigned>(b->B)), dim3(256), 0, st, true, b->LG, parts,
+                  static_cast<int64_t>(b->B) * V, static_cast<int64_t>(V), b->next);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return bfail(e, "batched forward");
     b->len += tps;
@@ -638,12 +689,24 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
     const int64_t T = static_cast<int64_t>(n_seqs) * max_tokens_per_seq;
     const int64_t kmax = std::max(H, F);
     const size_t cache = static_cast<size_t>(L) * n_seqs * max_ctx * KVD;
+    // Rows of partial tiles a matmul of n x k leaves over the token counts the
+    // batch runs (n_seqs x tokens_per_seq): split-K count x tokens, at most.
+    auto part_rows = [&](int64_t n, int64_t k) {
+        size_t rows = 0;
+        for (int64_t tps = 1; tps <= max_tokens_per_seq; ++tps) {
+            const int64_t tok = static_cast<int64_t>(n_seqs) * tps;
+            rows = std::max(rows, static_cast<size_t>(gemm_real_splits(k, gemm_splits(n, k, tok, b->sms)) * tok));
+        }
+        return rows;
+    };
     bool ok = balloc(b, cache * 4, &b->kc) && balloc(b, cache * 4, &b->vc) &&
               balloc(b, static_cast<size_t>(max_ctx) * 32 * 4, &b->rcos) &&
               balloc(b, static_cast<size_t>(max_ctx) * 32 * 4, &b->rsin) && balloc(b, T * H * 4, &b->X) &&
-              balloc(b, T * H * 4, &b->Y) &&
-              balloc(b, T * (H + 2 * KVD) * 4, &b->QKV) && balloc(b, T * H * 4, &b->ATT) &&
-              balloc(b, T * 2 * F * 4, &b->GU) && balloc(b, static_cast<size_t>(n_seqs) * V * 4, &b->LG) &&
+              balloc(b, std::max(part_rows(H, H), part_rows(H, F)) * H * 4, &b->Y) &&
+              balloc(b, part_rows(H + 2 * KVD, H) * (H + 2 * KVD) * 4, &b->QKV) && balloc(b, T * H * 4, &b->ATT) &&
+              balloc(b, part_rows(2 * F, H) * 2 * F * 4, &b->GU) &&
+              balloc(b, static_cast<size_t>(gemm_real_splits(H, gemm_splits(V, H, n_seqs, b->sms))) * n_seqs * V * 4,
+                     &b->LG) &&
               balloc(b, 16, &b->len_dev) &&
               balloc(b, static_cast<size_t>(gemm_x_plane_bytes(T, kmax)), &b->planes) &&
               balloc(b, static_cast<size_t>(gemm_tokens_padded(T)) * 4, &b->inv) &&

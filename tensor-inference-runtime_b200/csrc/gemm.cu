@@ -31,6 +31,7 @@
 
 #include "host.h"
 #include "launch.cuh"
+#include "parts.cuh"
 #include "ptx.cuh"
 #include "runtime.h"
 
@@ -44,7 +45,7 @@ constexpr int kGThreads = 192;
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
 constexpr int kGPlaneA = kGM * kGKS * 2;            // one f16 weight plane of a stage (16 KB)
 constexpr uint32_t kGErrTimeout = 25;
-constexpr int kGMaxSplits = 8;  // split-K CTAs of a tile: one cluster (portable size)
+constexpr int kGMaxSplits = 16;  // split-K CTAs per tile
 
 template <int NT>
 struct GemmCfg {
@@ -76,8 +77,8 @@ struct GemmParams {
     const float* w_pow2;     // [n rounded up to 128]: 2^kw of each row
     const uint8_t* xp;       // activation planes: [token tile][k step][hi | lo]
     const float* x_inv;      // [tokens rounded up to 128]: 2^-kx of each token
-    float* y;                // [tokens][y_ld]: the product (or y + the product, accumulate != 0)
-    int32_t n, k, tokens, y_ld, ks_per_split, accumulate;
+    float* y;                // [splits][tokens][y_ld]: the partial products of the K splits
+    int32_t n, k, tokens, y_ld, ks_per_split;
     uint32_t* err;
     unsigned long long timeout_ns;
 };
@@ -124,15 +125,20 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Bounded wait on an mbarrier phase; false (error recorded) on expiry.
+// Bounded wait on an mbarrier phase; false (error recorded) on expiry, or
+// at once when an earlier launch already recorded an error (so a failing
+// launch sequence ends quickly instead of timing out kernel by kernel).
 __device__ __forceinline__ bool gwait(const GemmParams& p, uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t n = 0;; ++n) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((n & 63u) == 63u && globaltimer_ns() - t0 > p.timeout_ns) {
-            atomicCAS(p.err, 0u, kGErrTimeout);
-            return false;
+        if ((n & 63u) == 63u) {
+            if (ld_relaxed_gpu(p.err) != 0u) return false;
+            if (globaltimer_ns() - t0 > p.timeout_ns) {
+                atomicCAS(p.err, 0u, kGErrTimeout);
+                return false;
+            }
         }
     }
 }
@@ -150,7 +156,6 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     const int nks_all = p.k / kGKS;
     const int ks0 = split * p.ks_per_split;
     const int nks = min(nks_all, ks0 + p.ks_per_split) - ks0;
-    const int splits = gridDim.z;  // launched as clusters of (1, 1, splits)
     if (tid == 0) {
         for (int i = 0; i < kRaw; ++i) {
             mbar_init(&s.full_w[i], 1);
@@ -302,73 +307,21 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         const int n = rt * kGM + row;
         const float inv_w = 1.0f / p.w_pow2[rt * kGM + row];
         const float* inv_x = s.inv_x;
-        if (acc_ok) {
-            // split-K: this CTA's partial tile goes to its own shared memory,
-            // token-major (the weight/activation rings are idle by now)
-            float* part = reinterpret_cast<float*>(s.a);
+        // split-K: CTA `split` stores its partial product as partial tile
+        // `split` of y ([splits][tokens][y_ld]); the reader adds them up
+        float* y = p.y + static_cast<size_t>(split) * p.tokens * p.y_ld;
+        if (acc_ok) {  // warp-uniform: the TMEM loads are warp-collective
             for (int c0 = 0; c0 < NT; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
-                float yv[16];  // accumulate: every load of the group before its stores
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int t = tt * NT + c0 + j;
-                    yv[j] = splits == 1 && p.accumulate && t < p.tokens && n < p.n
-                                ? p.y[static_cast<size_t>(t) * p.y_ld + n]
-                                : 0.f;
-                }
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int t = tt * NT + c0 + j;
-                    const float val = __uint_as_float(v[j]) * inv_x[c0 + j] * inv_w;
-                    if (splits > 1) {
-                        part[(c0 + j) * kGM + row] = val;
-                    } else if (t < p.tokens && n < p.n) {
-                        p.y[static_cast<size_t>(t) * p.y_ld + n] = p.accumulate ? __fadd_rn(yv[j], val) : val;
-                    }
+                    if (t < p.tokens && n < p.n)
+                        y[static_cast<size_t>(t) * p.y_ld + n] = __uint_as_float(v[j]) * inv_x[c0 + j] * inv_w;
                 }
             }
         }
-    }
-    if (splits > 1) {
-        // Split-K over the cluster of the tile's `splits` CTAs: once every
-        // partial tile is in place, CTA j sums token slice j of the tile over
-        // the CTAs' shared memory in rank order (deterministic) and writes it.
-        cluster_sync();
-        if (warp >= 2) {
-            const int row = (warp & 3) * 32 + lane;
-            const int n = rt * kGM + row;
-            const int t_end = min(NT, p.tokens - tt * NT);
-            const int t0 = split * t_end / splits, t1 = (split + 1) * t_end / splits;
-            const uint32_t base = smem_u32(s.a) + static_cast<uint32_t>(row) * 4u;
-            constexpr int U = 8;  // tokens per round: U x splits loads in flight
-            for (int t = t0; t < t1; t += U) {
-                float v[U][kGMaxSplits], yv[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    yv[u] = 0.f;
-                    if (t + u < t1) {
-                        const uint32_t la = base + static_cast<uint32_t>((t + u) * kGM) * 4u;
-#pragma unroll
-                        for (int sp = 0; sp < kGMaxSplits; ++sp)
-                            if (sp < splits) v[u][sp] = ld_dsmem_f32(dsmem_map(la, sp));
-                        if (p.accumulate && n < p.n) yv[u] = p.y[static_cast<size_t>(tt * NT + t + u) * p.y_ld + n];
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    if (t + u < t1 && n < p.n) {
-                        float acc = v[u][0];
-#pragma unroll
-                        for (int sp = 1; sp < kGMaxSplits; ++sp)
-                            if (sp < splits) acc = __fadd_rn(acc, v[u][sp]);
-                        p.y[static_cast<size_t>(tt * NT + t + u) * p.y_ld + n] =
-                            p.accumulate ? __fadd_rn(yv[u], acc) : acc;
-                    }
-                }
-            }
-        }
-        cluster_sync();  // no CTA leaves while a peer still reads its partial tile
     }
     tc_fence_before();
     __syncthreads();
@@ -496,9 +449,10 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_x_planes_kernel(const floa
 // multiplication by the correctly rounded reciprocal), h = row
 // rows ? rows[t] : t of X -- after X += Y on that row when Y is given (the
 // residual add of src/forward.rs, fused here so the matmul before it only
-// stores).
+// stores), Y the sum of y_parts partial tiles y_part floats apart.
 __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* __restrict__ X,
-                                                                         const float* __restrict__ Y,
+                                                                         float* __restrict__ Y, int y_parts,
+                                                                         int64_t y_part,
                                                                          const int32_t* __restrict__ rows,
                                                                          int64_t tokens, int64_t k,
                                                                          const float* __restrict__ w, float eps, int nt,
@@ -511,9 +465,11 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* 
     const bool live = t < tokens;
     const int64_t xr = live ? (rows ? static_cast<int64_t>(rows[t]) : t) : 0;
     float* x = X + xr * k;
-    if (live && Y) {
-        const float* y = Y + xr * k;
-        for (int64_t c = threadIdx.x; c < k; c += kPlaneThreads) x[c] = __fadd_rn(x[c], y[c]);
+    if (Y) {
+        float* y = Y + xr * k;  // partial tile 0 takes the sum
+        sum_parts_inplace(y, live ? y_parts : 1, y_part, static_cast<int>(k));
+        if (live)
+            for (int64_t c = threadIdx.x; c < k; c += kPlaneThreads) x[c] = __fadd_rn(x[c], y[c]);
         __syncthreads();
     }
     float ss = 0.f;
@@ -529,15 +485,18 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* 
 }
 
 // Planes of h[t][j] = silu(gate) * up from interleaved (gate_j, up_j) columns
-// of GU [tokens][2 f] (src/math.rs:171-175).
-__global__ void __launch_bounds__(kPlaneThreads) gemm_silu_planes_kernel(const float* __restrict__ gu, int64_t tokens,
-                                                                         int64_t f, int nt,
+// of GU [tokens][2 f] (src/math.rs:171-175), GU the sum of `parts` partial
+// tiles `part` floats apart.
+__global__ void __launch_bounds__(kPlaneThreads) gemm_silu_planes_kernel(float* __restrict__ gu, int parts,
+                                                                         int64_t part, int64_t tokens, int64_t f,
+                                                                         int nt,
                                                                          uint8_t* __restrict__ planes,
                                                                          float* __restrict__ inv) {
     griddep_launch_dependents();
     griddep_wait();
     const int64_t t = blockIdx.x;
-    const float* row = gu + t * 2 * f;
+    float* row = gu + t * 2 * f;  // partial tile 0 takes the sum
+    sum_parts_inplace(row, t < tokens ? parts : 1, part, static_cast<int>(2 * f));
     planes_row(
         [&](int64_t j) {
             const float2 p = *reinterpret_cast<const float2*>(row + 2 * j);
@@ -588,19 +547,20 @@ int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* pla
                                           gemm_token_tile(tokens), planes, inv));
 }
 
-int launch_gemm_norm_planes(float* X, const float* Y, const int32_t* rows, int64_t tokens, int64_t k, const float* w,
-                            float eps, uint8_t* planes, float* inv, void* stream, bool pdl) {
+int launch_gemm_norm_planes(float* X, float* Y, int y_parts, int64_t y_part, const int32_t* rows, int64_t tokens,
+                            int64_t k, const float* w, float eps, uint8_t* planes, float* inv, void* stream, bool pdl) {
     return static_cast<int>(launch_kernel(gemm_norm_planes_kernel,
                                           dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))), dim3(kPlaneThreads),
-                                          0, static_cast<cudaStream_t>(stream), pdl, X, Y, rows, tokens, k, w, eps,
+                                          0, static_cast<cudaStream_t>(stream), pdl, X, Y, y_parts, y_part, rows, tokens,
+                                          k, w, eps,
                                           gemm_token_tile(tokens), planes, inv));
 }
 
-int launch_gemm_silu_planes(const float* gu, int64_t tokens, int64_t f, uint8_t* planes, float* inv, void* stream,
-                            bool pdl) {
+int launch_gemm_silu_planes(float* gu, int parts, int64_t part, int64_t tokens, int64_t f, uint8_t* planes,
+                            float* inv, void* stream, bool pdl) {
     return static_cast<int>(launch_kernel(gemm_silu_planes_kernel,
                                           dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))), dim3(kPlaneThreads),
-                                          0, static_cast<cudaStream_t>(stream), pdl, gu, tokens, f,
+                                          0, static_cast<cudaStream_t>(stream), pdl, gu, parts, part, tokens, f,
                                           gemm_token_tile(tokens), planes, inv));
 }
 
@@ -627,79 +587,46 @@ int gemm_configure() {
     return 0;
 }
 
-namespace {
-
-// Clusters of `size` matmul CTAs (token tile nt) that can be resident at once
-// on the current device (cached; 0 when the query fails).
-int max_active_clusters(int nt, int size) {
-    static thread_local int dev_cached = -1;
-    static thread_local int cache[2][kGMaxSplits + 1];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    if (dev != dev_cached) {
-        for (auto& r : cache)
-            for (int& v : r) v = -1;
-        dev_cached = dev;
-    }
-    int& c = cache[nt == 64 ? 0 : 1][size];
-    if (c >= 0) return c;
-    if (gemm_configure() != 0) return 0;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(1, 1, static_cast<unsigned>(size));
-    cfg.blockDim = dim3(kGThreads);
-    cfg.dynamicSmemBytes = (nt == 64 ? sizeof(GemmSmem<64>) : sizeof(GemmSmem<256>)) + 1024;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 1;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = static_cast<unsigned>(size);
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    const cudaError_t e = nt == 64 ? cudaOccupancyMaxActiveClusters(&n, gemm_q8_kernel<64>, &cfg)
-                                   : cudaOccupancyMaxActiveClusters(&n, gemm_q8_kernel<256>, &cfg);
-    c = e == cudaSuccess ? n : 0;
-    return c;
+// K steps per split and the number of splits actually used when asking for
+// `splits` over k columns (every split non-empty).
+int gemm_real_splits(int64_t k, int splits) {
+    const int nks = static_cast<int>(k / kGKS);
+    splits = std::max(1, std::min({splits, nks, kGMaxSplits}));
+    const int per = (nks + splits - 1) / splits;
+    return (nks + per - 1) / per;
 }
-
-}  // namespace
 
 // Split-K factor for a matmul on `sms` multiprocessors (one CTA each): none
 // when the tiles alone fill the GPU, else the fewest waves of the shortest
-// CTAs, a wave being as many clusters of that size as fit at once, each CTA
-// paying about three K steps of pipeline fill.
+// CTAs, each CTA paying about three K steps of pipeline fill.
 int gemm_splits(int64_t n, int64_t k, int64_t tokens, int sms) {
     const int64_t tiles = gemm_tile_count(n, tokens), nks = k / kGKS;
     if (tiles <= 0 || nks <= 0 || sms <= 0 || tiles >= sms) return 1;
-    const int nt = gemm_token_tile(tokens);
     int best = 1;
     int64_t best_cost = (tiles + sms - 1) / sms * (nks + 3);
-    for (int64_t sp = 2; sp <= std::min<int64_t>(nks, kGMaxSplits); ++sp) {
-        const int64_t per = (nks + sp - 1) / sp, real = (nks + per - 1) / per;
-        if (real != sp) continue;
-        const int cap = max_active_clusters(nt, static_cast<int>(sp));
-        if (cap <= 0) continue;
-        const int64_t cost = (tiles + cap - 1) / cap * (per + 3);
+    for (int sp = 2; sp <= std::min<int64_t>(nks, kGMaxSplits); ++sp) {
+        if (gemm_real_splits(k, sp) != sp) continue;
+        const int64_t per = (nks + sp - 1) / sp;
+        const int64_t cost = (tiles * sp + sms - 1) / sms * (per + 3);
         if (cost < best_cost) {
             best_cost = cost;
-            best = static_cast<int>(sp);
+            best = sp;
         }
     }
     return best;
 }
 
-// y[t][n] (row stride y_ld) for t < tokens, n < n_rows, or y += that when
-// accumulate != 0.  splits > 1 (at most kGMaxSplits) divides K over that many
-// CTAs per tile, launched as one thread-block cluster that sums its partial
-// tiles in distributed shared memory.
+// Partial products of y[t][n] (row stride y_ld) for t < tokens, n < n_rows:
+// with s = gemm_real_splits(k, splits), partial j (K steps of split j) goes
+// to y + j * tokens * y_ld, and y is their sum in order j = 0 .. s - 1.
 int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes, const float* x_inv, int64_t n,
-                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int accumulate, int splits, uint32_t* err,
+                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int splits, uint32_t* err,
                    unsigned long long timeout_ns, void* stream, bool pdl) {
     const int cfg = gemm_configure();
     if (cfg != 0) return cfg;
     const int nt = gemm_token_tile(tokens);
     const int nks = static_cast<int>(k / kGKS);
-    splits = std::max(1, std::min({splits, nks, kGMaxSplits}));
+    splits = gemm_real_splits(k, splits);
     GemmParams p{};
     p.w = w;
     p.w_pow2 = w_pow2;
@@ -709,21 +636,37 @@ int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes,
     p.k = static_cast<int32_t>(k);
     p.tokens = static_cast<int32_t>(tokens);
     p.y_ld = static_cast<int32_t>(y_ld);
-    p.accumulate = accumulate ? 1 : 0;
     p.ks_per_split = (nks + splits - 1) / splits;
-    splits = (nks + p.ks_per_split - 1) / p.ks_per_split;
     p.y = y;
     p.err = err;
     p.timeout_ns = timeout_ns;
     const dim3 grid(static_cast<unsigned>((n + kGM - 1) / kGM), static_cast<unsigned>((tokens + nt - 1) / nt),
                     static_cast<unsigned>(splits));
-    const dim3 cluster(1, 1, static_cast<unsigned>(splits));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const cudaError_t e = nt == 64 ? launch_kernel_cluster(gemm_q8_kernel<64>, grid, dim3(kGThreads),
-                                                            sizeof(GemmSmem<64>) + 1024, st, pdl, cluster, p)
-                                   : launch_kernel_cluster(gemm_q8_kernel<256>, grid, dim3(kGThreads),
-                                                           sizeof(GemmSmem<256>) + 1024, st, pdl, cluster, p);
+    const cudaError_t e = nt == 64 ? launch_kernel(gemm_q8_kernel<64>, grid, dim3(kGThreads),
+                                                    sizeof(GemmSmem<64>) + 1024, st, pdl, p)
+                                   : launch_kernel(gemm_q8_kernel<256>, grid, dim3(kGThreads),
+                                                   sizeof(GemmSmem<256>) + 1024, st, pdl, p);
     return static_cast<int>(e);
+}
+
+// y[i] = sum of the `splits` partial tiles (stride `part` floats) at i, i < n.
+__global__ void gemm_sum_parts_kernel(const float* __restrict__ y_parts, int splits, int64_t part, int64_t n,
+                                      float* __restrict__ y) {
+    griddep_launch_dependents();
+    griddep_wait();
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float acc = y_parts[i];
+        for (int j = 1; j < splits; ++j) acc = __fadd_rn(acc, y_parts[j * part + i]);
+        y[i] = acc;
+    }
+}
+
+int launch_gemm_sum_parts(const float* y_parts, int splits, int64_t part, int64_t n, float* y, void* stream, bool pdl) {
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 8));
+    return static_cast<int>(launch_kernel(gemm_sum_parts_kernel, dim3(grid), dim3(256), 0,
+                                          static_cast<cudaStream_t>(stream), pdl, y_parts, splits, part, n, y));
 }
 
 }  // namespace tir

@@ -127,23 +127,33 @@ int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out
 int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream,
                          bool pdl = false);
 // Planes of rmsnorm(X[r]) * w, r = rows ? rows[t] : t for t < tokens, after
-// X[r] += Y[r] when Y is not null.
-int launch_gemm_norm_planes(float* X, const float* Y, const int32_t* rows, int64_t tokens, int64_t k, const float* w,
-                            float eps, uint8_t* planes, float* inv, void* stream, bool pdl = false);
-// Planes of silu(gate) * up from interleaved (gate, up) columns of gu [tokens][2 f].
-int launch_gemm_silu_planes(const float* gu, int64_t tokens, int64_t f, uint8_t* planes, float* inv, void* stream,
+// X[r] += Y[r] when Y is not null, Y the sum of y_parts partial tiles y_part
+// floats apart (summed into tile 0).
+int launch_gemm_norm_planes(float* X, float* Y, int y_parts, int64_t y_part, const int32_t* rows, int64_t tokens,
+                            int64_t k, const float* w, float eps, uint8_t* planes, float* inv, void* stream,
                             bool pdl = false);
+// Planes of silu(gate) * up from interleaved (gate, up) columns of gu
+// [tokens][2 f], the sum of `parts` partial tiles `part` floats apart
+// (summed into tile 0).
+int launch_gemm_silu_planes(float* gu, int parts, int64_t part, int64_t tokens, int64_t f, uint8_t* planes,
+                            float* inv, void* stream, bool pdl = false);
 // Shared-memory opt-in of the matmul kernels on the current device (0 or a cudaError_t).
 int gemm_configure();
 // Weight-row tiles x token tiles of a matmul of n rows over `tokens` rows.
 int64_t gemm_tile_count(int64_t n, int64_t tokens);
-// Split-K factor for a matmul on `sms` multiprocessors.
+// Split-K factor for a matmul on `sms` multiprocessors, and the number of
+// splits (partial tiles) a request for `splits` yields.
 int gemm_splits(int64_t n, int64_t k, int64_t tokens, int sms);
-// y (row stride y_ld) = the matmul of the planes with the prepared weights,
-// or y += it (accumulate); split-K over `splits` CTAs per tile (one cluster).
+int gemm_real_splits(int64_t k, int splits);
+// Partial products of y = the planes' rows x the prepared weights: partial j
+// of s = gemm_real_splits(k, splits) at y + j * tokens * y_ld (y is their sum
+// in order).
 int launch_gemm_q8(const uint8_t* w, const float* w_pow2, const uint8_t* planes, const float* x_inv, int64_t n,
-                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int accumulate, int splits, uint32_t* err,
+                   int64_t k, int64_t tokens, float* y, int64_t y_ld, int splits, uint32_t* err,
                    unsigned long long timeout_ns, void* stream, bool pdl = false);
+// y[i] = sum of `splits` partial tiles (stride `part` floats), i < n.
+int launch_gemm_sum_parts(const float* y_parts, int splits, int64_t part, int64_t n, float* y, void* stream,
+                          bool pdl = false);
 
 // Rows per weight tile of a matrix with k columns (0: unsupported k).
 int tile_rows_for(int64_t k, bool pairs);

@@ -66,24 +66,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
-// Thread-block clusters: barrier over every thread of the cluster (release /
-// acquire: shared-memory writes before it are visible to peers after it), the
-// shared::cluster address of a local shared variable in CTA `rank`, and a load
-// through such an address (distributed shared memory).
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t dsmem_map(uint32_t local_smem_addr, int rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-    return v;
-}
-
 // Programmatic dependent launch.  griddep_wait: returns once every grid this
 // one depends on programmatically has completed and its memory is visible (at
 // once when launched without that dependency).  griddep_launch_dependents:
