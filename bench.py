@@ -429,7 +429,7 @@ def run_batched(args, dist):
     info = model.info
     V = info["vocab"]
     if args.workload == "batched":
-        B, P, cap = 64, 128, 128
+        B, P, cap = 64, 128, args.decode  # --decode shortens the run for profiling (default 128)
     else:
         B, P, cap = 16, 512, 0
     rng = np.random.default_rng(args.seed + 7919 * dist.rank)
