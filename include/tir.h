@@ -268,6 +268,13 @@ tir_status tir_q8_matmul_batch(const float *x, int64_t tokens, const uint8_t *w,
  * Streaming sm_100a GEMV over the split layout. */
 tir_status tir_q8_matmul(const float *x, const uint8_t *quants, const uint16_t *scales,
                          float *out, int64_t n, int64_t k, void *stream);
+/* matmul in Mode::Quantize (src/forward.rs:266-273): the f32 input quantised
+ * per 32 values by activated_q8 (src/kernels.rs:8-31), then q8_act_matmul
+ * (src/math.rs:101-112) -- exact integer block dots times the f16 activation
+ * scale and the weight scale -- on the split layout; the same input staging
+ * and block dot as the fused decode kernel's Mode::Quantize phases. */
+tir_status tir_q8_matmul_qact(const float *x, const uint8_t *quants, const uint16_t *scales, float *out,
+                              int64_t n, int64_t k, void *stream);
 /* q8_full_dequant / q8_dequant_block (src/math.rs:117-137): bit-exact. */
 tir_status tir_q8_dequant(const uint8_t *blocks, int64_t n_blocks, float *out, void *stream);
 /* embed (src/tokenizer.rs:10-32): row `id` of a Q8_0 [vocab][dim] table. */

@@ -104,7 +104,7 @@ static unsigned long long timeout_ns() {
 }
 
 tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out, int64_t n,
-                            int64_t k, void* stream) {
+                            int64_t k, void* stream, bool qact) {
     if (n == 0) return TIR_OK;
     int dev = 0;
     CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
@@ -122,6 +122,8 @@ tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_
     d.rows_per_tile = tile_rows_for(k, false);
     d.n_tiles = static_cast<int32_t>((n + d.rows_per_tile - 1) / d.rows_per_tile);
     d.tiled = scales == nullptr ? 1 : 0;
+    d.qact = qact ? 1 : 0;
+    p.qact = d.qact;
     d.wq = quants;
     d.ws = scales;
     d.in = x;
@@ -168,6 +170,7 @@ struct tir_state {
     int32_t *prompt = nullptr, *out_ids = nullptr, *tmp_id = nullptr;
     PhaseDesc* d_phases = nullptr;
     int n_phases = 0;
+    int32_t mode = 0;  // the model's mode the phase table was built for
     int32_t len = 0;
     bool dump_on = false;
     unsigned long long* trace = nullptr;
@@ -550,7 +553,7 @@ tir_status tir_model_info(const tir_model* m, tir_transformer* out) {
 
 tir_status tir_model_set_mode(tir_model* m, int32_t mode) {
     if (!m) return fail(TIR_ERR_INVALID_ARG, "null argument");
-    if (mode != 0) return fail(TIR_ERR_INVALID_ARG, "Mode::Quantize is not available in the fused decode path yet");
+    if (mode != 0 && mode != 1) return fail(TIR_ERR_INVALID_ARG, "mode must be 0 (Normal) or 1 (Quantize)");
     m->t.mode = mode;
     return TIR_OK;
 }
@@ -588,9 +591,13 @@ static tir_status build_phases(tir_state* s) {
         d.out = out;
         return d;
     };
+    // Mode::Quantize (src/forward.rs:261-275) quantises the input of the
+    // q, k, v, o and lm_head matmuls; the FFN always runs q8_matmul.
+    const int32_t qact = t.mode == 1 ? 1 : 0;
     for (int64_t l = 0; l < L; ++l) {
         PhaseDesc q = gemv(m->qkv[l], static_cast<int>(l), l == 0 ? IN_X0_NORM : IN_X_NORM, s->x, m->attn_norm[l],
                            EPI_QKV, s->q);
+        q.qact = qact;
         q.kc = s->kc + l * layer_cache;
         q.vc = s->vc + l * layer_cache;
         ph.push_back(q);
@@ -600,16 +607,28 @@ static tir_status build_phases(tir_state* s) {
         a.kc = q.kc;
         a.vc = q.vc;
         ph.push_back(a);
-        ph.push_back(gemv(m->o[l], static_cast<int>(l), IN_ATTN, s->attn, nullptr, EPI_RESID, s->x));
+        PhaseDesc o = gemv(m->o[l], static_cast<int>(l), IN_ATTN, s->attn, nullptr, EPI_RESID, s->x);
+        o.qact = qact;
+        ph.push_back(o);
         ph.push_back(gemv(m->gu[l], static_cast<int>(l), IN_X_NORM, s->x, m->ffn_norm[l], EPI_GU, s->h));
         PhaseDesc dn = gemv(m->down[l], static_cast<int>(l), IN_RAW, s->h, nullptr, EPI_RESID, s->x);
         dn.dump = 1;
         ph.push_back(dn);
     }
-    ph.push_back(gemv(m->lm, -1, L == 0 ? IN_X0_NORM : IN_X_NORM, s->x, m->out_norm, EPI_LOGITS, s->logits));
+    PhaseDesc lm = gemv(m->lm, -1, L == 0 ? IN_X0_NORM : IN_X_NORM, s->x, m->out_norm, EPI_LOGITS, s->logits);
+    lm.qact = qact;
+    ph.push_back(lm);
     (void)H;
     (void)KVD;
+    if (s->d_phases) {  // the model's mode changed since: same shapes, new table
+        CUDA_TRY(cudaStreamSynchronize(s->stream), "phase table update");
+        CUDA_TRY(cudaMemcpy(s->d_phases, ph.data(), ph.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice),
+                 "phase table upload");
+        s->mode = t.mode;
+        return TIR_OK;
+    }
     s->n_phases = static_cast<int>(ph.size());
+    s->mode = t.mode;
     void* p = nullptr;
     CUDA_TRY(cudaMalloc(&p, ph.size() * sizeof(PhaseDesc)), "phase table");
     s->allocs.push_back(p);
@@ -713,6 +732,10 @@ void tir_state_destroy(tir_state* s) { delete s; }
 static tir_status launch_steps(tir_state* s, int n_steps, int pos0, const float* x0, const int32_t* prompt,
                                int n_prompt, int32_t* out_ids) {
     const tir_transformer& t = s->m->t;
+    if (s->mode != t.mode) {  // tir_model_set_mode since the table was built
+        const tir_status rc = build_phases(s);
+        if (rc != TIR_OK) return rc;
+    }
     DecodeParams p{};
     p.phases = s->d_phases;
     p.n_phases = s->n_phases;
@@ -726,6 +749,7 @@ static tir_status launch_steps(tir_state* s, int n_steps, int pos0, const float*
     p.max_ctx = s->max_ctx;
     p.vocab = static_cast<int32_t>(t.vocab);
     p.max_splits = s->max_splits;
+    p.qact = t.mode == 1 ? 1 : 0;
     p.x0 = x0;
     p.prompt = prompt;
     p.n_prompt = n_prompt;
@@ -974,6 +998,16 @@ tir_status tir_q8_matmul(const float* x, const uint8_t* quants, const uint16_t* 
     if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
     if (!quants || !scales) return fail(TIR_ERR_INVALID_ARG, "null weights");
     return q8_matmul_stream(x, quants, scales, out, n, k, stream);
+}
+
+tir_status tir_q8_matmul_qact(const float* x, const uint8_t* quants, const uint16_t* scales, float* out, int64_t n,
+                              int64_t k, void* stream) {
+    clear_error();
+    if (n < 0 || k <= 0 || k % 32 != 0 || k > kMaxK)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "q8 matvec needs 0 < k <= " + std::to_string(kMaxK) + ", k % 32 == 0");
+    if (n > INT32_MAX / 2) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "too many rows");
+    if (!quants || !scales) return fail(TIR_ERR_INVALID_ARG, "null weights");
+    return q8_matmul_stream(x, quants, scales, out, n, k, stream, true);
 }
 
 int64_t tir_q8_tile_rows(int64_t k) { return tile_rows_for(k, false); }

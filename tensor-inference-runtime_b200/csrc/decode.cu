@@ -484,13 +484,12 @@ __device__ __forceinline__ void pack_digits(const uint32_t* u, uint32_t& w0, uin
 // (q = d0 + 256 d1 + 65536 d2, |d2| <= 64).  Blocks with m < 2^-86 use E = -86.
 // For the step input, the CTA owning a chunk also materialises it as the
 // residual stream x (and dump row 0).
-__device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
-                                            const Prefetch& pf) {
+__device__ __forceinline__ void stage_load(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
+                                           const Prefetch& pf, float* v, float& inv, float& rms) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = d.k, nchunks = K / 16;
     const bool norm = d.in_kind == IN_X_NORM || d.in_kind == IN_X0_NORM;
     const int c = tid;
-    float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = 0.f;
     if (d.in_kind == IN_ATTN && st.S <= kReaderCombineMaxSplits) {
@@ -528,7 +527,8 @@ __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, cons
             if (d4) d4[j] = t;
         }
     }
-    float inv = 1.0f;
+    inv = 1.0f;
+    rms = 1.0f;
     if (norm) {
         float ss = 0.f;
 #pragma unroll
@@ -539,10 +539,18 @@ __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, cons
         float total = 0.f;
 #pragma unroll
         for (int w = 0; w < kWarps; ++w) total += s.red[w];
-        inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), p.rms_eps)));
+        rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), p.rms_eps));
+        inv = __frcp_rn(rms);
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], pf.wr[i]);
     }
+}
+
+__device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
+                                            const Prefetch& pf) {
+    const int c = threadIdx.x, nchunks = d.k / 16;
+    float v[16], inv, rms;
+    stage_load(p, s, d, st, pf, v, inv, rms);
     float mx = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
@@ -567,6 +575,60 @@ __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, cons
     }
     cbar();
 }
+
+// Mode::Quantize input staging (src/forward.rs:261-275): the phase input as
+// stage_load leaves it, divided by rmsnorm's r (as the reference rounds it),
+// then the block's Q8_0 quantisation by activated_q8 (src/kernels.rs:8-31) --
+// scale = the signed element of largest |x| (the last of equal ones) / 127,
+// q = round(x / scale) half away from zero, saturated to int8, NaN -> 0 -- as
+// digit plane 0 (planes 1 and 2 zero), and the f16-rounded scale the block
+// dot multiplies by (dot_prod_act_q8, src/math.rs:39-50): unit_dot then yields
+// the exact integer block dot times scale_a * scale_w.  Compiled only into
+// the kernel instantiation for Mode::Quantize (decode_kernel<true>).
+__device__ __forceinline__ void stage_input_qact(const DecodeParams& p, Smem& s, const PhaseDesc& d,
+                                                 const StepCtx& st, const Prefetch& pf) {
+    const int c = threadIdx.x, nchunks = d.k / 16;
+    float v[16], inv, rms;
+    stage_load(p, s, d, st, pf, v, inv, rms);
+    uint32_t babs = 0u;
+    float bval = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        v[i] = __fdiv_rn(v[i], rms);
+        const uint32_t a = __float_as_uint(v[i]) & 0x7fffffffu;
+        if (a >= babs) {
+            babs = a;
+            bval = v[i];
+        }
+    }
+    const uint32_t oabs = __shfl_xor_sync(FULL, babs, 1);
+    const float oval = __shfl_xor_sync(FULL, bval, 1);
+    const int h = c & 1;  // half 1 follows half 0 in the block: it wins ties
+    if (h == 0 ? oabs >= babs : oabs > babs) bval = oval;
+    const float scale = __fdiv_rn(bval, 127.0f);
+    if (c < nchunks) {
+        uint32_t w0[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            uint32_t word = 0u;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float r = roundf(__fdiv_rn(v[4 * g + e], scale));
+                const int qi = r != r ? 0 : static_cast<int>(fminf(fmaxf(r, -128.0f), 127.0f));
+                word |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * e);
+            }
+            w0[g] = word;
+        }
+        const int b = c >> 1;
+        *reinterpret_cast<uint4*>(&s.u.st.xd[0][b][4 * h]) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+        *reinterpret_cast<uint4*>(&s.u.st.xd[1][b][4 * h]) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(&s.u.st.xd[2][b][4 * h]) = make_uint4(0u, 0u, 0u, 0u);
+        if (h == 0) s.u.st.xsc[b] = __half2float(__float2half_rn(scale));
+    }
+    (void)inv;
+    cbar();
+}
+
 
 // Sums eight per-lane values over the warp with 9 shuffles; lane l ends with
 // the total of value (l >> 2) & 7.
@@ -748,6 +810,7 @@ __device__ __forceinline__ bool gemv_tiles(const DecodeParams& p, Smem& s, Strea
 
 // One GEMV phase; returns false on timeout (this CTA then stops at the end
 // of the phase, together with its other warps).
+template <bool QACT>
 __device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, Stream& sw, const PhaseDesc& d,
                                            const StepCtx& st, int ph, uint32_t gidx, const Prefetch& pf,
                                            TraceAcc& tr) {
@@ -757,7 +820,10 @@ __device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, Strea
         if (d.epi == EPI_LOGITS && tid == 0) p.argmax_part[blockIdx.x] = 0ull;
         return true;
     }
-    stage_input(p, s, d, st, pf);
+    if (QACT && d.qact)
+        stage_input_qact(p, s, d, st, pf);
+    else
+        stage_input(p, s, d, st, pf);
     trace_mark(p, ph, st.f, 2);
     unsigned long long best = 0ull;
     bool ok;
@@ -940,6 +1006,7 @@ __device__ __forceinline__ bool attn_prefetch(const DecodeParams& p, Smem& s, co
 // ---------------------------------------------------------------------------
 // the program loop
 // ---------------------------------------------------------------------------
+template <bool QACT>
 __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) {
     const int G = gridDim.x;
     const int tid = threadIdx.x;
@@ -1010,7 +1077,7 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
                     st.token = s.token;
                     st.x0_given = (f == 0 && p.x0 != nullptr);
                 }
-                ok = gemv_phase(p, s, sw, d, st, ph, gidx, pf, tr);
+                ok = gemv_phase<QACT>(p, s, sw, d, st, ph, gidx, pf, tr);
                 gidx += static_cast<uint32_t>(s.nmine[ph]);
             }
             if (!ok) s.abort_flag = 1;  // any warp: the CTA stops after this phase
@@ -1043,6 +1110,9 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
     }
 }
 
+// QACT: the instantiation that also runs Mode::Quantize phases (PhaseDesc.qact);
+// the Normal-mode one carries none of that code.
+template <bool QACT>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
@@ -1059,18 +1129,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     Stream sw{Pos{0, 0, 0}, true, -1, nullptr, 0, 0};
     sw.more = s.nmine[0] > 0 || pos_advance(p, s, sw.c, 0);
     for (uint32_t i = 0; i < static_cast<uint32_t>(kWarpSlots); ++i) stream_next(p, s, sw, i, warp, lane);
-    run(p, s, sw);
+    run<QACT>(p, s, sw);
     cp_async_wait_all();
 }
 
 int decode_smem_bytes() { return static_cast<int>(sizeof(Smem)); }
 
 int decode_blocks_per_sm() {
-    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(sizeof(Smem))) != cudaSuccess)
         return 0;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel, kThreads, sizeof(Smem)) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<false>, kThreads, sizeof(Smem)) != cudaSuccess)
         return 0;
     return n;
 }
@@ -1081,23 +1151,28 @@ int decode_grid_size(int device) {
     return sms;
 }
 
+// p.qact selects the instantiation that runs Mode::Quantize phases.
 int decode_launch(const DecodeParams& p, int grid, void* stream, bool cooperative) {
     static thread_local int configured_device = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_device != dev) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(sizeof(Smem)));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(sizeof(Smem)));
         if (e != cudaSuccess) return static_cast<int>(e);
         configured_device = dev;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void (*kernel)(DecodeParams) = p.qact ? decode_kernel<true> : decode_kernel<false>;
     if (cooperative) {
         void* args[] = {const_cast<DecodeParams*>(&p)};
-        return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(decode_kernel), dim3(grid),
+        return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<void*>(kernel), dim3(grid),
                                                             dim3(kThreads), args, sizeof(Smem), st));
     }
-    decode_kernel<<<grid, kThreads, sizeof(Smem), st>>>(p);
+    kernel<<<grid, kThreads, sizeof(Smem), st>>>(p);
     return static_cast<int>(cudaGetLastError());
 }
 

@@ -115,7 +115,7 @@ int launch_fill_f32(float* out, float v, int64_t n, void* stream);
 // Streaming Q8_0 matvec (decode.cu machinery, one phase) over the split
 // layout (quants, scales) or, with scales == NULL, the tile-major layout.
 tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out,
-                            int64_t n, int64_t k, void* stream);
+                            int64_t n, int64_t k, void* stream, bool qact = false);
 
 // Batched Q8_0 matmul on the tensor cores (gemm.cu).
 int64_t gemm_q8_weight_bytes(int64_t n, int64_t k);

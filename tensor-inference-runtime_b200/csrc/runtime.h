@@ -85,6 +85,7 @@ struct PhaseDesc {
     int32_t rows_per_tile, n_tiles;  // rows_per_tile = gemv_tile_rows(k)
     int32_t dump;              // EPI_RESID: also write the residual to the dump
     int32_t tiled;             // 1: wq is warp-sliced tile-major (q8_slice_offset), ws unused
+    int32_t qact;              // 1: Mode::Quantize input -- activated_q8 blocks, integer block dots
     const uint8_t* wq;         // quants [n][k] signed int8 q (split layout), or the tiled matrix
     const uint16_t* ws;        // f16 scales [n][sk] (split layout)
     const float* in;           // IN_RAW input / IN_X_NORM residual buffer
@@ -100,6 +101,7 @@ struct DecodeParams {
     int32_t n_phases;
     int32_t n_steps, pos0;
     int32_t H, q_heads, kv_heads, group, kvd, max_ctx, vocab, max_splits;
+    int32_t qact;              // some phase runs Mode::Quantize (PhaseDesc.qact): that kernel instantiation
     // token source of each step (IN_X0_NORM): x0 (step 0 only, optional),
     // else prompt[f] for f < n_prompt, else argmax of the previous logits.
     const float* x0;

@@ -107,6 +107,7 @@ SIGNATURES = {
     "tir_q8_scale_stride": (_i64, [_i64]),
     "tir_q8_repack": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "tir_q8_matmul": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "tir_q8_matmul_qact": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_q8_dequant": (C.c_int, [_vp, _i64, _vp, _vp]),
     "tir_embed": (C.c_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
     "tir_rmsnorm": (C.c_int, [_vp, _vp, _vp, _i64, _vp]),
@@ -443,6 +444,11 @@ def q8_repack(blocks, rows, k, quants, scales, stream=None):
 
 def q8_matmul(x, quants, scales, out, n, k, stream=None):
     check(lib().tir_q8_matmul(_ptr(x), _ptr(quants), _ptr(scales), _ptr(out), n, k, _stream(stream)))
+
+
+def q8_matmul_qact(x, quants, scales, out, n, k, stream=None):
+    """matmul in Mode::Quantize (src/forward.rs:266-273) from an f32 input."""
+    check(lib().tir_q8_matmul_qact(_ptr(x), _ptr(quants), _ptr(scales), _ptr(out), n, k, _stream(stream)))
 
 
 class Batch:

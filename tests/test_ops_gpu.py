@@ -272,6 +272,25 @@ def test_q8_act_matmul_bit_exact(cuda, tirlib, orc, k, n):
     np.testing.assert_array_equal(host(out), orc.q8_act_matmul(xq, blocks.reshape(-1), n))
 
 
+@pytest.mark.parametrize("k,n,case", [(2048, 2048, "random"), (1024, 1536, "random"), (512, 768, "random"),
+                                      (5632, 64, "random"), (2048, 300, "ties"), (1024, 96, "zeros")])
+def test_q8_matmul_qact_vs_oracle(cuda, tirlib, orc, k, n, case):
+    """The fused kernel's Mode::Quantize input staging and integer block dot
+    (single-phase launch) against activated_q8 + q8_act_matmul: the same
+    per-block terms, summed in another order (rel-L2 below 1e-6)."""
+    torch = cuda
+    x, blocks = synth.gemv_case(k, n, seed=7 * k + n)
+    if case == "ties":  # equal |x| of opposite signs: the last one sets the scale's sign
+        x[3], x[9], x[40], x[41] = 4.0, -4.0, -2.0, 2.0
+    elif case == "zeros":
+        x[:64] = 0.0
+    q, s = split_layout(torch, tirlib, blocks, n, k)
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
+    tirlib.q8_matmul_qact(dev(torch, x), q, s, out, n, k)
+    ref = orc.q8_act_matmul(orc.activated_q8(x), blocks.reshape(-1), n)
+    assert rel_l2(host(out), ref) < 1e-6
+
+
 @pytest.mark.parametrize("case", ["random", "ties", "nan", "zeros", "empty", "big"])
 def test_argmax_matches_sample(cuda, tirlib, orc, case):
     torch = cuda
