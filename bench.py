@@ -238,6 +238,36 @@ def cpu_baseline(args):
             "sample": f"first {n_prompt} prompt ids + {cap} greedy steps of the workload (16 forwards)"}
 
 
+def cpu_baseline_batched(args):
+    """Oracle on the host cores for the batched workloads, on the samples the
+    measurement plan names: the batched decode workload on 2 of its sequences
+    (each 128 prompt ids + 128 greedy steps), the prefill workload on one of
+    its 512-id sequences -- the reference runs sequences one after another and
+    feeds prompts token by token, so tok/s = forwards / wall time."""
+    from oracle import load_oracle
+    from oracle.gguf_ref import GGUF
+    from tir import synth
+    import numpy as np
+    orc = load_oracle()
+    orc.set_threads(host_threads())
+    om = orc.model(GGUF(synth.synthetic_model("tinyllama", args.seed)))
+    rng = np.random.default_rng(args.seed)
+    if args.workload == "batched":
+        seqs, P, cap = 2, 128, args.decode
+        sample = f"2 of the 64 sequences, each {P} prompt ids + {cap} greedy steps ({seqs * (P + cap)} forwards)"
+    else:
+        seqs, P, cap = 1, 512, 0
+        sample = "one of the 16 sequences: 512 prompt ids fed token by token (512 forwards)"
+    prompts = rng.integers(3, 32000, size=(seqs, P), dtype=np.int32)
+    om.generate_capped(prompts[0, :1], 0)  # page the weights in
+    t0 = time.perf_counter()
+    for s_ in range(seqs):
+        om.generate_capped(prompts[s_], cap)
+    dt = time.perf_counter() - t0
+    return {"value": seqs * (P + cap) / dt, "unit": "tok/s", "cores": orc.get_threads(), "kind": "port",
+            "sample": sample}
+
+
 def run_ours(args, dist):
     import numpy as np
     import torch
@@ -464,6 +494,13 @@ def run_batched(args, dist):
     e2e_ms = dist.max(wall_ms)
     forwards = P + cap
     tokens = B * forwards * dist.world
+    # kernels of one step: a multi-token forward is the embedding, 10 per layer
+    # (norm planes, q|k|v matmul, RoPE + KV append, attention, planes, o
+    # matmul, norm planes, gate|up matmul, SiLU planes, down matmul) and 4 at
+    # the end (last rows, final norm planes, lm_head matmul, argmax); a decode
+    # forward has no separate RoPE launch, plus the id feedback kernel
+    L_ = info["layers"]
+    launches_per_step = (1 + 10 * L_ + 4) + cap * (1 + 9 * L_ + 4 + 1)
     wb = model.weight_bytes()
     if args.workload == "batched":
         name = (f"TinyLlama-1.1B-shape Q8_0 model, {B} sequences per GPU, each {P} seeded prompt ids (one batched "
@@ -505,9 +542,11 @@ def run_batched(args, dist):
             "roofline": roof,
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * P * 4,
                     "d2h_bytes_per_step": B * cap * 4 + 4},
-            "gpu_launches": None, "clocks": clocks.summary()}
+            "gpu_launches": args.steps * launches_per_step, "clocks": clocks.summary()}
     batch.close()
     model.close()
+    if args.cpu_baseline == "auto" and dist.world == 1:
+        line["cpu_baseline"] = cpu_baseline_batched(args)
     return line
 
 

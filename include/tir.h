@@ -210,6 +210,35 @@ tir_status tir_state_enable_trace(tir_state *s, int32_t step);
 tir_status tir_state_trace_dims(const tir_state *s, int32_t *n_phases, int32_t *grid);
 tir_status tir_state_trace(tir_state *s, uint64_t *out_host);
 
+/* ---- text: tokenizer and text drivers (src/tokenizer.rs:37-150, src/lib.rs:140-314)
+ * Host-side BPE over the GGUF's tokenizer.ggml.tokens / tokenizer.ggml.merges. */
+typedef struct tir_tokenizer tir_tokenizer;
+/* MissingField / WrongType as the drivers report them (src/lib.rs:149-160,
+ * src/tokenizer.rs:42-48). */
+tir_status tir_tokenizer_create(const tir_gguf *g, tir_tokenizer **out);
+/* From caller arrays (token / merge strings with their byte lengths). */
+tir_status tir_tokenizer_create_from(const char *const *tokens, const uint64_t *token_lens, int64_t n_tokens,
+                                     const char *const *merges, const uint64_t *merge_lens, int64_t n_merges,
+                                     tir_tokenizer **out);
+void tir_tokenizer_destroy(tir_tokenizer *t);
+int64_t tir_tokenizer_vocab_size(const tir_tokenizer *t);
+/* encode (src/tokenizer.rs:37-120): BOS 1, then the BPE ids of `text`
+ * (UTF-8, text_len bytes).  *n gets the id count; up to cap ids are written. */
+tir_status tir_encode(const tir_tokenizer *t, const char *text, int64_t text_len, int32_t *ids, int64_t cap,
+                      int64_t *n);
+/* decode (src/tokenizer.rs:122-143): TIR_ERR_BAD_TOKEN on an id outside the
+ * vocab (UnknownId).  *len gets the byte length; up to cap - 1 bytes and a NUL
+ * are written. */
+tir_status tir_decode(const tir_tokenizer *t, const int32_t *ids, int64_t n_ids, char *out, int64_t cap,
+                      int64_t *len);
+/* generate_capped on text (src/lib.rs:239-314): out_ids_host [cap]. */
+tir_status tir_generate_capped_text(tir_state *s, const tir_tokenizer *tk, const char *text, int64_t text_len,
+                                    int32_t cap, int32_t *out_ids_host);
+/* generate (src/lib.rs:140-236): greedy until id 13 or 2 (not kept), at most
+ * max_new ids; the kept ids decoded into out_text. */
+tir_status tir_generate_text(tir_state *s, const tir_tokenizer *tk, const char *text, int64_t text_len,
+                             int32_t max_new, char *out_text, int64_t cap, int64_t *out_len, int32_t *n_ids);
+
 /* ---- batched sequences: many tokens per forward --------------------------- */
 /* n_seqs independent sequences advancing in lockstep (batched greedy decode and
  * batched prefill); each sequence computes what generate_capped

@@ -892,6 +892,45 @@ tir_status tir_generate_capped(tir_state* s, const int32_t* prompt_host, int32_t
     return TIR_OK;
 }
 
+// generate_capped on text (src/lib.rs:239-314): encode (BOS + BPE ids), the
+// prompt fed token by token, then cap greedy ids.
+tir_status tir_generate_capped_text(tir_state* s, const tir_tokenizer* tk, const char* text, int64_t text_len,
+                                    int32_t cap, int32_t* out_ids_host) {
+    clear_error();
+    if (!s || !tk) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    int64_t n = 0;
+    tir_status rc = tir_encode(tk, text, text_len, nullptr, 0, &n);
+    if (rc != TIR_OK) return rc;
+    std::vector<int32_t> ids(static_cast<size_t>(n));
+    rc = tir_encode(tk, text, text_len, ids.data(), n, &n);
+    if (rc != TIR_OK) return rc;
+    return tir_generate_capped(s, ids.data(), static_cast<int32_t>(n), cap, out_ids_host, nullptr);
+}
+
+// generate (src/lib.rs:140-236): encode, the prompt token by token, then
+// greedy ids until id 13 (newline) or 2 (EOS), which is not kept; the ids
+// before it decoded to text.  The reference loops without bound; here at
+// most max_new ids are generated (one device launch of max_new steps, cut at
+// the first stop id).  *n_ids gets the number of ids kept.
+tir_status tir_generate_text(tir_state* s, const tir_tokenizer* tk, const char* text, int64_t text_len,
+                             int32_t max_new, char* out_text, int64_t cap, int64_t* out_len, int32_t* n_ids) {
+    clear_error();
+    if (!s || !tk || max_new < 0) return fail(TIR_ERR_INVALID_ARG, "null argument or negative max_new");
+    int64_t n = 0;
+    tir_status rc = tir_encode(tk, text, text_len, nullptr, 0, &n);
+    if (rc != TIR_OK) return rc;
+    std::vector<int32_t> prompt(static_cast<size_t>(n));
+    rc = tir_encode(tk, text, text_len, prompt.data(), n, &n);
+    if (rc != TIR_OK) return rc;
+    std::vector<int32_t> gen(static_cast<size_t>(std::max(max_new, 1)));
+    rc = tir_generate_capped(s, prompt.data(), static_cast<int32_t>(n), max_new, gen.data(), nullptr);
+    if (rc != TIR_OK) return rc;
+    int32_t kept = 0;
+    while (kept < max_new && gen[static_cast<size_t>(kept)] != 13 && gen[static_cast<size_t>(kept)] != 2) ++kept;
+    if (n_ids) *n_ids = kept;
+    return tir_decode(tk, gen.data(), kept, out_text, cap, out_len);
+}
+
 tir_status tir_state_sync(tir_state* s) {
     clear_error();
     if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");

@@ -70,6 +70,16 @@ SIGNATURES = {
     "tir_last_error": (C.c_char_p, []),
     "tir_version": (C.c_char_p, []),
     "tir_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "tir_tokenizer_create": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "tir_tokenizer_create_from": (C.c_int, [C.POINTER(C.c_char_p), C.POINTER(C.c_uint64), _i64,
+                                            C.POINTER(C.c_char_p), C.POINTER(C.c_uint64), _i64, C.POINTER(_vp)]),
+    "tir_tokenizer_destroy": (None, [_vp]),
+    "tir_tokenizer_vocab_size": (_i64, [_vp]),
+    "tir_encode": (C.c_int, [_vp, C.c_char_p, _i64, _i32p, _i64, C.POINTER(_i64)]),
+    "tir_decode": (C.c_int, [_vp, _i32p, _i64, C.c_char_p, _i64, C.POINTER(_i64)]),
+    "tir_generate_capped_text": (C.c_int, [_vp, _vp, C.c_char_p, _i64, C.c_int32, _i32p]),
+    "tir_generate_text": (C.c_int, [_vp, _vp, C.c_char_p, _i64, C.c_int32, C.c_char_p, _i64, C.POINTER(_i64),
+                                    C.POINTER(C.c_int32)]),
     "tir_gguf_open_bytes": (C.c_int, [_vp, _sz, C.POINTER(_vp)]),
     "tir_gguf_close": (None, [_vp]),
     "tir_gguf_parse_general": (C.c_int, [_vp, _sz, _sz, C.c_uint64, C.POINTER(_vp), C.POINTER(_sz)]),
@@ -298,6 +308,64 @@ def parse_q8(count, byte_count, map_len, offset):
 # ---------------------------------------------------------------------------
 # Model / State
 # ---------------------------------------------------------------------------
+class Tokenizer:
+    """BPE encode / decode (src/tokenizer.rs:37-150) over a vocab and merge list."""
+
+    def __init__(self, handle):
+        self._h = handle
+        self._destroy = lib().tir_tokenizer_destroy  # held by the object: usable at interpreter teardown
+
+    @classmethod
+    def from_gguf(cls, gguf):
+        h = _vp()
+        check(lib().tir_tokenizer_create(gguf.handle, C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_lists(cls, tokens, merges):
+        tb = [t.encode("utf-8") for t in tokens]
+        mb = [m.encode("utf-8") for m in merges]
+        tp = (C.c_char_p * max(len(tb), 1))(*tb)
+        tl = (C.c_uint64 * max(len(tb), 1))(*[len(b) for b in tb])
+        mp = (C.c_char_p * max(len(mb), 1))(*mb)
+        ml = (C.c_uint64 * max(len(mb), 1))(*[len(b) for b in mb])
+        h = _vp()
+        check(lib().tir_tokenizer_create_from(tp, tl, len(tb), mp, ml, len(mb), C.byref(h)))
+        return cls(h)
+
+    def close(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self._h = None
+            self._destroy(h)
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def handle(self):
+        return self._h
+
+    def __len__(self):
+        return int(lib().tir_tokenizer_vocab_size(self._h))
+
+    def encode(self, text):
+        raw = text.encode("utf-8") if isinstance(text, str) else bytes(text)
+        n = _i64()
+        check(lib().tir_encode(self._h, raw, len(raw), None, 0, C.byref(n)))
+        out = np.zeros(max(n.value, 1), np.int32)
+        check(lib().tir_encode(self._h, raw, len(raw), out.ctypes.data_as(_i32p), n.value, C.byref(n)))
+        return out[:n.value]
+
+    def decode(self, ids):
+        ids = np.ascontiguousarray(ids, np.int32)
+        n = _i64()
+        check(lib().tir_decode(self._h, ids.ctypes.data_as(_i32p), ids.size, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value + 1)
+        check(lib().tir_decode(self._h, ids.ctypes.data_as(_i32p), ids.size, buf, n.value + 1, C.byref(n)))
+        return buf.raw[:n.value].decode("utf-8")
+
+
 class Model:
     """Weights resident in HBM (load_model, src/lib.rs:29-138)."""
 
@@ -399,6 +467,25 @@ class State:
                                         out.ctypes.data_as(_i32p),
                                         logits.ctypes.data_as(_f32p) if want_logits else None))
         return (out[:cap], logits) if want_logits else out[:cap]
+
+    def generate_capped_text(self, tokenizer, text, cap):
+        """generate_capped (src/lib.rs:239-314) on text."""
+        raw = text.encode("utf-8")
+        out = np.zeros(max(cap, 1), np.int32)
+        check(lib().tir_generate_capped_text(self._h, tokenizer.handle, raw, len(raw), cap,
+                                             out.ctypes.data_as(_i32p)))
+        return out[:cap]
+
+    def generate_text(self, tokenizer, text, max_new):
+        """generate (src/lib.rs:140-236): greedy until id 13 or 2, at most max_new ids.
+        Returns (text, number of ids kept)."""
+        raw = text.encode("utf-8")
+        n, k = _i64(), C.c_int32()
+        cap = 64 * max(max_new, 1) + 1
+        buf = C.create_string_buffer(cap)
+        check(lib().tir_generate_text(self._h, tokenizer.handle, raw, len(raw), max_new, buf, cap,
+                                      C.byref(n), C.byref(k)))
+        return buf.raw[:min(n.value, cap - 1)].decode("utf-8"), k.value
 
     def generate_capped_device(self, prompt_dev, n_prompt, cap, out_dev):
         check(lib().tir_generate_capped_device(self._h, _ptr(prompt_dev), n_prompt, cap,

@@ -35,7 +35,7 @@ PRESETS = {
                  ffn_dim=1408, vocab=1000, rope_theta=10000.0, rms_eps=1e-5, ctx=512),
 }
 
-_T_U32, _T_F32, _T_STRING = 4, 6, 8
+_T_U32, _T_F32, _T_STRING, _T_ARRAY = 4, 6, 8, 9
 
 
 def _rng(seed, name):
@@ -98,6 +98,38 @@ def _nbytes(dtype, shape):
     return n * 4 if dtype == 0 else n // 32 * 34
 
 
+SPACE = "\u2581"  # sentencepiece's word-boundary mark
+
+
+def synthetic_tokenizer(vocab):
+    """A BPE vocabulary of `vocab` tokens and its merge list, shaped like a
+    llama sentencepiece tokenizer: <unk>, <s>, </s>, the 256 byte tokens
+    <0x00>..<0xFF>, the word mark, a-z, mark+letter, letter pairs, then
+    filler pieces.  Synthetic: it exercises encode/decode and the text
+    drivers, not any real language."""
+    letters = [chr(c) for c in range(ord("a"), ord("z") + 1)]
+    toks = ["<unk>", "<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)] + [SPACE] + letters
+    merges = []
+    for l in letters:
+        toks.append(SPACE + l)
+        merges.append(f"{SPACE} {l}")
+    for a in "etaoinshr":
+        for b in "etaoinshr":
+            toks.append(a + b)
+            merges.append(f"{a} {b}")
+            toks.append(SPACE + a + b)
+            merges.append(f"{SPACE}{a} {b}")
+    i = 0
+    while len(toks) < vocab:
+        toks.append(f"{SPACE}w{i}")
+        i += 1
+    return toks[:vocab], merges
+
+
+def _gguf_string_array(values):
+    return struct.pack("<IQ", _T_STRING, len(values)) + b"".join(_gguf_string(v) for v in values)
+
+
 def write_gguf(path, cfg, seed=0):
     """Writes the synthetic model ``cfg`` (a PRESETS entry) to ``path``."""
     meta = [("general.architecture", _T_STRING, "llama"),
@@ -113,6 +145,10 @@ def write_gguf(path, cfg, seed=0):
             ("llama.rope.freq_base", _T_F32, cfg["rope_theta"]),
             ("llama.attention.layer_norm_rms_epsilon", _T_F32, cfg["rms_eps"]),
             ("general.file_type", _T_U32, 7)]
+    toks, merges = synthetic_tokenizer(cfg["vocab"])
+    meta += [("tokenizer.ggml.model", _T_STRING, "llama"),
+             ("tokenizer.ggml.tokens", _T_ARRAY, toks),
+             ("tokenizer.ggml.merges", _T_ARRAY, merges)]
     specs = tensor_specs(cfg)
     head = bytearray(GGUF_MAGIC + struct.pack("<IQQ", 3, len(specs), len(meta)))
     for name, t, v in meta:
@@ -121,6 +157,8 @@ def write_gguf(path, cfg, seed=0):
             head += struct.pack("<I", v)
         elif t == _T_F32:
             head += struct.pack("<f", v)
+        elif t == _T_ARRAY:
+            head += _gguf_string_array(v)
         else:
             head += _gguf_string(v)
     offset = 0
@@ -155,7 +193,7 @@ def cache_dir():
 
 def synthetic_model(preset="tinyllama", seed=0):
     """Path of the cached synthetic GGUF for (preset, seed), written on first use."""
-    path = os.path.join(cache_dir(), f"{preset}-q8_0-seed{seed}.gguf")
+    path = os.path.join(cache_dir(), f"{preset}-q8_0-seed{seed}-tok.gguf")
     if not os.path.exists(path):
         write_gguf(path, PRESETS[preset], seed)
     return path
