@@ -240,24 +240,42 @@ tir_status tir_generate_text(tir_state *s, const tir_tokenizer *tk, const char *
                              int32_t max_new, char *out_text, int64_t cap, int64_t *out_len, int32_t *n_ids);
 
 /* ---- batched sequences: many tokens per forward --------------------------- */
-/* n_seqs independent sequences advancing in lockstep (batched greedy decode and
- * batched prefill); each sequence computes what generate_capped
- * (src/lib.rs:239-314) computes for it alone, with every projection on the
- * tensor cores (tir_q8_matmul_batch).  The batch keeps its own KV caches
- * (n_seqs x max_ctx positions) and a tensor-core copy of the model's weights. */
+/* n_seqs sequences, each computing what generate_capped (src/lib.rs:239-314)
+ * computes for it alone, with every projection on the tensor cores
+ * (tir_q8_matmul_batch).  The KV cache (replacing the unbounded Cache,
+ * src/data.rs:41-51) is paged: positions in pages of 16 from a pool shared by
+ * the sequences, taken as a sequence grows and returned when it is reset, so
+ * sequences of different lengths share the memory (continuous batching).
+ * The batch keeps a tensor-core copy of the model's weights. */
 typedef struct tir_batch tir_batch;
+/* A pool of n_pages pages (16 positions each, all layers). */
+tir_status tir_batch_create_paged(tir_model *m, int32_t n_seqs, int32_t max_ctx, int32_t max_tokens_per_seq,
+                                  int32_t n_pages, tir_batch **out);
+/* The pool every sequence can fill to max_ctx at once. */
 tir_status tir_batch_create(tir_model *m, int32_t n_seqs, int32_t max_ctx, int32_t max_tokens_per_seq,
                             tir_batch **out);
 void tir_batch_destroy(tir_batch *b);
+/* Every sequence / sequence `seq` empty again (its pages back in the pool). */
 tir_status tir_batch_reset(tir_batch *b);
+tir_status tir_batch_reset_seq(tir_batch *b, int32_t seq);
+/* The longest sequence's length; sequence `seq`'s length; free pool pages. */
 int32_t tir_batch_len(const tir_batch *b);
+int32_t tir_batch_seq_len(const tir_batch *b, int32_t seq);
+int32_t tir_batch_free_pages(const tir_batch *b);
 void *tir_batch_stream(tir_batch *b);
-/* Appends tokens_per_seq ids to every sequence (ids_host [n_seqs][tokens_per_seq])
- * and returns each sequence's greedy next id (next_ids_host [n_seqs], may be NULL). */
+/* counts_host[s] new ids for sequence s (0: idle this step, > 1: a prompt
+ * chunk, mixed freely), ids_host their concatenation in sequence order;
+ * next_ids_host [n_seqs] (may be NULL) gets each sequence's greedy next id
+ * (meaningless for idle ones).  TIR_ERR_CTX_OVERFLOW past max_ctx, TIR_ERR_OOM
+ * when the pool runs short (nothing changes then). */
+tir_status tir_batch_step_ragged(tir_batch *b, const int32_t *ids_host, const int32_t *counts_host,
+                                 int32_t *next_ids_host);
+/* tokens_per_seq ids for every sequence (ids_host [n_seqs][tokens_per_seq]). */
 tir_status tir_batch_step(tir_batch *b, const int32_t *ids_host, int32_t tokens_per_seq,
                           int32_t *next_ids_host);
-/* Per sequence: prompt (prompts_host [n_seqs][n_prompt]) then cap greedy steps,
- * n_prompt + cap forwards as generate_capped; out_ids_host [n_seqs][cap]. */
+/* Per sequence from empty: prompt (prompts_host [n_seqs][n_prompt]) then cap
+ * greedy steps, n_prompt + cap forwards as generate_capped; out_ids_host
+ * [n_seqs][cap]. */
 tir_status tir_batch_generate(tir_batch *b, const int32_t *prompts_host, int32_t n_prompt, int32_t cap,
                               int32_t *out_ids_host);
 

@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -24,6 +25,26 @@ namespace {
 
 constexpr uint32_t kBErrBadToken = 12;
 constexpr int kQBlock = 32;   // query tokens per prefill attention CTA (one per lane)
+constexpr int kPage = 16;     // KV-cache positions per page
+
+// A step's row layout and the paged KV cache.  Row r of the step's q|k|v (and
+// attention output) is token r - seq_row0[s] of sequence s = row_seq[r], at
+// position seq_len[s] + that index; position p of sequence s lives in page
+// table[s * max_pages + p / kPage], slot p % kPage.  The cache of one layer
+// is [pages][kPage][kvd] floats for K and the same for V.
+struct Pages {
+    int32_t* seq_len;         // [n_seqs] tokens before this step (advanced at its end)
+    const int32_t* seq_row0;  // [n_seqs] first row of the sequence's new tokens
+    const int32_t* seq_cnt;   // [n_seqs] new tokens this step (0: idle)
+    const int32_t* row_seq;   // [rows] sequence of each row
+    const int32_t* table;     // [n_seqs][max_pages]
+    int32_t max_pages;
+};
+
+__device__ __forceinline__ size_t kv_slot(const Pages& pg, int s, int pos, int kvd) {
+    const int page = pg.table[static_cast<size_t>(s) * pg.max_pages + pos / kPage];
+    return (static_cast<size_t>(page) * kPage + pos % kPage) * kvd;
+}
 
 // Q8_0 blocks of a matrix held in the decode kernel's warp-sliced tile-major
 // layout (runtime.h q8_slice_offset), written back as [n][k/32] 34-byte blocks.
@@ -66,22 +87,22 @@ __global__ void embed_rows_kernel(const int32_t* __restrict__ ids, const uint8_t
     }
 }
 
-// RoPE on the q and k parts of each token's fused q|k|v row (src/math.rs:196-228),
-// then the KV-cache append (src/forward.rs:83-84).  Token t belongs to
-// sequence t / tps at position *pos0 + t % tps; cache [seq][max_ctx][kvd].
-__global__ void rope_append_kernel(float* __restrict__ qkv, int parts, int64_t part, int64_t ld, int tps,
-                                   const int32_t* pos0, int H, int kvd, int max_ctx, const float* __restrict__ rc,
-                                   const float* __restrict__ rs, float* __restrict__ kc, float* __restrict__ vc) {
+// RoPE on the q and k parts of each row's fused q|k|v (src/math.rs:196-228),
+// then the KV-cache append (src/forward.rs:83-84) at the row's sequence and
+// position (Pages).
+__global__ void rope_append_kernel(float* __restrict__ qkv, int parts, int64_t part, int64_t ld, Pages pg, int H,
+                                   int kvd, const float* __restrict__ rc, const float* __restrict__ rs,
+                                   float* __restrict__ kc, float* __restrict__ vc) {
     griddep_launch_dependents();
     griddep_wait();
     const int64_t t = blockIdx.x;
-    const int64_t s = t / tps;
-    const int pos = *pos0 + static_cast<int>(t % tps);
+    const int s = pg.row_seq[t];
+    const int pos = pg.seq_len[s] + static_cast<int>(t - pg.seq_row0[s]);
     float* row = qkv + t * ld;
     // the q|k|v row: the sum of the matmul's partial tiles (into tile 0)
     sum_parts_inplace(row, parts, part, H + 2 * kvd);
     auto val = [&](int c) { return row[c]; };
-    const size_t cache_row = (static_cast<size_t>(s) * max_ctx + pos) * kvd;
+    const size_t cache_row = kv_slot(pg, s, pos, kvd);
     for (int pr = threadIdx.x; pr < (H + kvd) / 2; pr += blockDim.x) {
         const int c = 2 * pr;
         const int i = (c % kHeadDim) >> 1;
@@ -112,24 +133,27 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int parts, int64_t p
 constexpr int kPChunk = 64;
 constexpr int kPHeads = 8;  // query heads (warps) per CTA
 
-__global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const float* __restrict__ qkv, int64_t ld, int tps,
-                                                              const int32_t* pos0p, int H, int kvd, int group,
-                                                              int max_ctx, const float* __restrict__ kc,
-                                                              const float* __restrict__ vc, float* __restrict__ out) {
+__global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const float* __restrict__ qkv, int64_t ld,
+                                                                      Pages pg, int H, int kvd, int group,
+                                                                      const float* __restrict__ kc,
+                                                                      const float* __restrict__ vc,
+                                                                      float* __restrict__ out) {
     griddep_launch_dependents();
     griddep_wait();
     __shared__ __align__(16) float4 ks[kPChunk][kHeadDim / 4];
     __shared__ __align__(16) float4 vs[kPChunk][kHeadDim / 4];
     const int n_hb = (group + kPHeads - 1) / kPHeads;
     const int s = blockIdx.x, g = blockIdx.y / n_hb, hb = blockIdx.y % n_hb, qb = blockIdx.z;
+    const int cnt = pg.seq_cnt[s];
+    if (qb * kQBlock >= cnt) return;  // the whole CTA: no query of this sequence in the block
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hg = hb * kPHeads + warp;  // query head within the group
     const int h = g * group + hg;
     const int qi = qb * kQBlock + lane;  // query token within the sequence's new tokens
-    const bool active = qi < tps && hg < group;
-    const int pos0 = *pos0p;
+    const bool active = qi < cnt && hg < group;
+    const int pos0 = pg.seq_len[s];
     const int qpos = pos0 + qi;
-    const int64_t t = static_cast<int64_t>(s) * tps + qi;
+    const int64_t t = static_cast<int64_t>(pg.seq_row0[s]) + qi;
     float q[kHeadDim], o[kHeadDim];
 #pragma unroll
     for (int d = 0; d < kHeadDim; ++d) {
@@ -137,14 +161,13 @@ __global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const flo
         o[d] = 0.f;
     }
     float m = -INFINITY, l = 0.f;
-    const int last = pos0 + min(tps, (qb + 1) * kQBlock) - 1;  // the block's last query position
-    const size_t head_base = static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
+    const int last = pos0 + min(cnt, (qb + 1) * kQBlock) - 1;  // the block's last query position
     for (int c0 = 0; c0 <= last; c0 += kPChunk) {
         __syncthreads();
         for (int e = threadIdx.x; e < kPChunk * (kHeadDim / 4); e += blockDim.x) {
             const int j = e / (kHeadDim / 4), d4 = e % (kHeadDim / 4);
             const bool in = c0 + j <= last;
-            const size_t off = head_base + static_cast<size_t>(c0 + j) * kvd;
+            const size_t off = in ? kv_slot(pg, s, c0 + j, kvd) + static_cast<size_t>(g) * kHeadDim : 0;
             ks[j][d4] = in ? reinterpret_cast<const float4*>(kc + off)[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
             vs[j][d4] = in ? reinterpret_cast<const float4*>(vc + off)[d4] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
@@ -246,9 +269,8 @@ constexpr int kMaxParts = 16;  // split-K partial tiles a reader sums
 
 template <int G>  // query heads per kv head, rounded up (heads >= group are computed on zeros, not stored)
 __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const float* __restrict__ qkv, int parts,
-                                                                      int64_t part, int64_t ld,
-                                                                      const int32_t* posp, int H, int kvd, int group,
-                                                                      int max_ctx, const float* __restrict__ rc,
+                                                                      int64_t part, int64_t ld, Pages pg, int H,
+                                                                      int kvd, int group, const float* __restrict__ rc,
                                                                       const float* __restrict__ rs,
                                                                       float* __restrict__ kc,
                                                                       float* __restrict__ vc,
@@ -259,9 +281,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
     __shared__ float ms[kAttnWarps][G], ls[kAttnWarps][G];
     __shared__ float os[kAttnWarps][G][kHeadDim];
     const int s = blockIdx.x, g = blockIdx.y;
+    if (pg.seq_cnt[s] == 0) return;  // the whole CTA: the sequence is idle this step
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = *posp;
-    const float* row = qkv + static_cast<int64_t>(s) * ld;
+    const int pos = pg.seq_len[s];
+    const int64_t r = pg.seq_row0[s];  // the sequence's row in this step
+    const float* row = qkv + r * ld;
     auto val = [&](int c) {  // partial loads first, then the sum in partial order
         float v[kMaxParts];
 #pragma unroll
@@ -272,7 +296,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
             if (j < parts) acc = __fadd_rn(acc, v[j]);
         return acc;
     };
-    const size_t cache_row = (static_cast<size_t>(s) * max_ctx + pos) * kvd + static_cast<size_t>(g) * kHeadDim;
+    const size_t head = static_cast<size_t>(g) * kHeadDim;
+    const size_t cache_row = kv_slot(pg, s, pos, kvd) + head;
     for (int pr = threadIdx.x; pr < (group + 1) * (kHeadDim / 2); pr += blockDim.x) {
         const bool isq = pr < group * (kHeadDim / 2);
         const int i = pr % (kHeadDim / 2);  // rotation pair within the head
@@ -302,15 +327,13 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
         o1[h] = 0.f;
     }
     const int n = pos + 1;
-    const float* kb = kc + static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
-    const float* vb = vc + static_cast<size_t>(s) * max_ctx * kvd + static_cast<size_t>(g) * kHeadDim;
     for (int c0 = warp * 32; c0 < n; c0 += kAttnWarps * 32) {
         const int j = c0 + lane;
         const bool valid = j < n;
         float p[G];
 #pragma unroll
         for (int h = 0; h < G; ++h) p[h] = 0.f;
-        const float4* kr = reinterpret_cast<const float4*>(kb + static_cast<size_t>(valid ? j : c0) * kvd);
+        const float4* kr = reinterpret_cast<const float4*>(kc + kv_slot(pg, s, valid ? j : c0, kvd) + head);
 #pragma unroll 4
         for (int i = 0; i < kHeadDim / 4; ++i) {
             const float4 kv = kr[i];
@@ -344,7 +367,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
         }
         const int nc = min(32, n - c0);
         for (int jj = 0; jj < nc; ++jj) {
-            const float* vr = vb + static_cast<size_t>(c0 + jj) * kvd;
+            const float* vr = vc + kv_slot(pg, s, c0 + jj, kvd) + head;
             const float v0 = vr[lane], v1 = vr[lane + 32];
 #pragma unroll
             for (int h = 0; h < G; ++h) {
@@ -376,7 +399,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
             L = fmaf(ls[w][h], f, L);
             O = fmaf(os[w][h][d], f, O);
         }
-        out[static_cast<int64_t>(s) * H + (g * group + h) * kHeadDim + d] = O / L;
+        out[r * H + (g * group + h) * kHeadDim + d] = O / L;
     }
 }
 
@@ -406,14 +429,18 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int parts, int64
     }
 }
 
-// Each sequence's last new row; the device length advances by tps (every
-// kernel of the forward that reads it has run by now).
-__global__ void last_rows_kernel(int32_t* rows, int n_seqs, int tps, int32_t* len) {
+// Each sequence's last new row (row 0 for an idle sequence, whose logits are
+// not used); then every sequence's device length advances by its new tokens
+// (every kernel of the forward that reads it has run by now).
+__global__ void last_rows_kernel(int32_t* rows, Pages pg, int n_seqs) {
     griddep_launch_dependents();
     griddep_wait();
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s < n_seqs) rows[s] = s * tps + tps - 1;
-    if (s == 0) *len += tps;
+    if (s < n_seqs) {
+        const int cnt = pg.seq_cnt[s];
+        rows[s] = cnt > 0 ? pg.seq_row0[s] + cnt - 1 : 0;
+        pg.seq_len[s] += cnt;
+    }
 }
 
 // Greedy decode feedback: the sampled ids are both the next input and
@@ -443,20 +470,32 @@ struct tir_batch {
         int64_t n = 0, k = 0;
     };
     tir_model* m = nullptr;
-    int B = 0, max_ctx = 0, max_tps = 0, len = 0, sms = 148;
+    int B = 0, max_ctx = 0, max_tps = 0, sms = 148;
+    int max_pages = 0, n_pages = 0;  // pages per sequence at most; pages in the pool
     cudaStream_t stream = nullptr;
     std::vector<void*> allocs;
     std::vector<GW> qkv, o, gu, down;
     GW lm;
-    float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr;
+    float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr;  // kc, vc: [layers][n_pages][kPage][kvd]
     float *X = nullptr, *Y = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *LG = nullptr, *inv = nullptr;
     uint8_t* planes = nullptr;
     int32_t *ids = nullptr, *rows = nullptr, *next = nullptr, *h_next = nullptr;
     uint32_t *err = nullptr, *h_err = nullptr;
-    int32_t* len_dev = nullptr;  // the sequences' length on the device (kernels read it: graph replays stay valid)
-    int32_t* gen = nullptr;      // generated ids [gen_cap][B] (tir_batch_generate)
+    // Sequences and pages.  seq_len lives on the device (kernels read and
+    // advance it, so graph replays stay valid); h_len mirrors it.
+    int32_t* seq_len = nullptr;
+    std::vector<int32_t> h_len;
+    std::vector<std::vector<int32_t>> seq_pages;  // pages of each sequence, in position order
+    std::vector<int32_t> free_pages;
+    int32_t *table = nullptr, *h_table = nullptr;  // [B][max_pages], device and pinned host
+    bool table_dirty = false;
+    // Step layouts ([row0 B | cnt B | row_seq]): dyn for any step (pinned
+    // host copy h_dyn), uni = every sequence one token (constant; the decode
+    // graph reads it).
+    int32_t *dyn = nullptr, *h_dyn = nullptr, *uni = nullptr;
+    int32_t* gen = nullptr;  // generated ids [gen_cap][B] (tir_batch_generate)
     int gen_cap = 0;
-    cudaGraphExec_t decode_graph = nullptr;  // one decode forward (tps = 1) + id feedback, captured on first use
+    cudaGraphExec_t decode_graph = nullptr;  // one decode forward on `uni`, captured on first use
     ~tir_batch() {
         cudaSetDevice(m ? m->device : 0);
         if (stream) cudaStreamSynchronize(stream);
@@ -465,6 +504,8 @@ struct tir_batch {
         for (void* p : allocs) cudaFree(p);
         if (h_next) cudaFreeHost(h_next);
         if (h_err) cudaFreeHost(h_err);
+        if (h_table) cudaFreeHost(h_table);
+        if (h_dyn) cudaFreeHost(h_dyn);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -517,15 +558,28 @@ tir_status planes_rc(int rc) {
     return rc == 0 ? TIR_OK : bfail(static_cast<cudaError_t>(rc), "activation planes");
 }
 
+// The step layout `meta` ([row0 B | cnt B | row_seq]) as kernel arguments.
+Pages pages_of(tir_batch* b, const int32_t* meta) {
+    Pages pg;
+    pg.seq_len = b->seq_len;
+    pg.seq_row0 = meta;
+    pg.seq_cnt = meta + b->B;
+    pg.row_seq = meta + 2 * b->B;
+    pg.table = b->table;
+    pg.max_pages = b->max_pages;
+    return pg;
+}
+
 // Decode attention (with the q|k|v partial sum, RoPE and KV append) over the
 // group size rounded up to an instantiated width.
-void attn_decode(tir_batch* b, int parts, int group, int kv_heads, int H, int KVD, int64_t ldq, float* kc, float* vc) {
+void attn_decode(tir_batch* b, const Pages& pg, int64_t rows, int parts, int group, int kv_heads, int H, int KVD,
+                 int64_t ldq, float* kc, float* vc) {
     const dim3 grid(static_cast<unsigned>(b->B), static_cast<unsigned>(kv_heads));
     const unsigned th = kAttnWarps * 32;
-    const int64_t part = static_cast<int64_t>(b->B) * ldq;
-#define TIR_ATTN(GM)                                                                                                 \
-    launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, parts, part, ldq, b->len_dev, H, \
-                  KVD, group, b->max_ctx, b->rcos, b->rsin, kc, vc, b->ATT)
+    const int64_t part = rows * ldq;
+#define TIR_ATTN(GM)                                                                                                   \
+    launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, parts, part, ldq, pg, H, KVD,    \
+                  group, b->rcos, b->rsin, kc, vc, b->ATT)
     if (group <= 1)
         TIR_ATTN(1);
     else if (group <= 2)
@@ -539,21 +593,23 @@ void attn_decode(tir_batch* b, int parts, int group, int kv_heads, int H, int KV
 #undef TIR_ATTN
 }
 
-// One forward over tps new tokens of every sequence (ids already in b->ids,
-// sequence-major); greedy next id of every sequence into b->next.  Per
-// layer: the previous layer's residual add + rmsnorm fused into the
-// activation planes of the q|k|v matmul, RoPE + KV append, attention, the o
-// matmul (into Y), residual add + rmsnorm into the gate|up planes, SiLU * up
-// into the down planes, the down matmul (into Y, added by the next norm).
-tir_status forward(tir_batch* b, int tps) {
+// One forward over the step layout `meta` (T rows; ids already in b->ids,
+// sequence-major); greedy next id of every sequence into b->next.
+// max_cnt: the most new tokens of one sequence (1: the decode attention, which
+// also does RoPE and the KV append).  Per layer: the previous layer's residual
+// add + rmsnorm fused into the activation planes of the q|k|v matmul, RoPE +
+// KV append, attention, the o matmul (into Y), residual add + rmsnorm into the
+// gate|up planes, SiLU * up into the down planes, the down matmul (into Y,
+// added by the next norm).
+tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
     tir_model* m = b->m;
     const tir_transformer& t = m->t;
     const int H = static_cast<int>(t.embed_dim), KVD = static_cast<int>(t.kv_dim), F = static_cast<int>(t.ffn_dim);
     const int V = static_cast<int>(t.vocab), L = static_cast<int>(t.layers);
     const int group = static_cast<int>(t.q_heads / t.k_v_heads);
-    const int64_t T = static_cast<int64_t>(b->B) * tps;
     const int64_t ldq = H + 2 * KVD;
-    const size_t layer_cache = static_cast<size_t>(b->B) * b->max_ctx * KVD;
+    const size_t layer_cache = static_cast<size_t>(b->n_pages) * kPage * KVD;
+    const Pages pg = pages_of(b, meta);
     cudaStream_t st = b->stream;
     tir_status rc;
     launch_kernel(embed_rows_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->ids, m->embd.q,
@@ -567,16 +623,15 @@ tir_status forward(tir_batch* b, int tps) {
         if ((rc = mm(b, T, b->qkv[l], b->QKV, &parts)) != TIR_OK) return rc;
         float* kc = b->kc + l * layer_cache;
         float* vc = b->vc + l * layer_cache;
-        if (tps == 1) {
-            attn_decode(b, parts, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);
+        if (max_cnt <= 1) {
+            attn_decode(b, pg, T, parts, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);
         } else {
             launch_kernel(rope_append_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->QKV, parts,
-                          T * ldq, ldq, tps, b->len_dev, H, KVD, b->max_ctx, b->rcos, b->rsin, kc, vc);
+                          T * ldq, ldq, pg, H, KVD, b->rcos, b->rsin, kc, vc);
             launch_kernel(attn_prefill_kernel,
                           dim3(b->B, static_cast<unsigned>(t.k_v_heads * ((group + kPHeads - 1) / kPHeads)),
-                               (tps + kQBlock - 1) / kQBlock),
-                          dim3(kPHeads * 32), 0, st, true, b->QKV, ldq, tps, b->len_dev, H, KVD, group, b->max_ctx, kc,
-                          vc, b->ATT);
+                               (max_cnt + kQBlock - 1) / kQBlock),
+                          dim3(kPHeads * 32), 0, st, true, b->QKV, ldq, pg, H, KVD, group, kc, vc, b->ATT);
         }
         if ((rc = planes_rc(launch_gemm_x_planes(b->ATT, T, H, b->planes, b->inv, st, true))) != TIR_OK) return rc;
         if ((rc = mm(b, T, b->o[l], b->Y, &y_parts)) != TIR_OK) return rc;
@@ -589,7 +644,7 @@ tir_status forward(tir_batch* b, int tps) {
             return rc;
         if ((rc = mm(b, T, b->down[l], b->Y, &y_parts)) != TIR_OK) return rc;
     }
-    launch_kernel(last_rows_kernel, dim3((b->B + 127) / 128), dim3(128), 0, st, true, b->rows, b->B, tps, b->len_dev);
+    launch_kernel(last_rows_kernel, dim3((b->B + 127) / 128), dim3(128), 0, st, true, b->rows, pg, b->B);
     // the last down projection's residual add, on the rows the logits need
     if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, y_parts, T * H, b->rows, b->B, H, m->out_norm, 1e-5f,
                                                 b->planes, b->inv, st, true))) != TIR_OK)
@@ -599,21 +654,66 @@ tir_status forward(tir_batch* b, int tps) {
                   static_cast<int64_t>(b->B) * V, static_cast<int64_t>(V), b->next);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return bfail(e, "batched forward");
-    b->len += tps;
     return TIR_OK;
 }
 
-// forward(b, 1) through a CUDA graph captured on first use: the launch
-// sequence of a decode step depends only on the batch's buffers, and every
-// kernel reads the position from the device.
+// Pages for positions [0, new_len) of sequence s, from the pool; TIR_ERR_OOM
+// (nothing taken) when the pool runs short.
+tir_status ensure_pages(tir_batch* b, int s, int new_len) {
+    const size_t need = static_cast<size_t>((new_len + kPage - 1) / kPage);
+    std::vector<int32_t>& mine = b->seq_pages[static_cast<size_t>(s)];
+    if (need <= mine.size()) return TIR_OK;
+    if (need - mine.size() > b->free_pages.size()) return fail(TIR_ERR_OOM, "the batch's KV page pool is exhausted");
+    while (mine.size() < need) {
+        const int32_t pgid = b->free_pages.back();
+        b->free_pages.pop_back();
+        b->h_table[static_cast<size_t>(s) * b->max_pages + mine.size()] = pgid;
+        mine.push_back(pgid);
+    }
+    b->table_dirty = true;
+    return TIR_OK;
+}
+
+tir_status upload_table(tir_batch* b) {
+    if (!b->table_dirty) return TIR_OK;
+    const cudaError_t e = cudaMemcpyAsync(b->table, b->h_table, static_cast<size_t>(b->B) * b->max_pages * 4,
+                                          cudaMemcpyHostToDevice, b->stream);
+    if (e != cudaSuccess) return bfail(e, "page table upload");
+    b->table_dirty = false;
+    return TIR_OK;
+}
+
+// Sequence s empties: its pages back to the pool, its length 0 (host and device).
+tir_status release_seq(tir_batch* b, int s) {
+    std::vector<int32_t>& mine = b->seq_pages[static_cast<size_t>(s)];
+    for (auto it = mine.rbegin(); it != mine.rend(); ++it) b->free_pages.push_back(*it);
+    mine.clear();
+    b->h_len[static_cast<size_t>(s)] = 0;
+    const cudaError_t e = cudaMemsetAsync(b->seq_len + s, 0, 4, b->stream);
+    return e == cudaSuccess ? TIR_OK : bfail(e, "sequence reset");
+}
+
+// Every sequence empty.  Pages may still be in use by queued work: the
+// stream is drained first.
+tir_status reset_all(tir_batch* b) {
+    cudaError_t e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return bfail(e, "batch reset");
+    for (int s = 0; s < b->B; ++s) {
+        const tir_status rc = release_seq(b, s);
+        if (rc != TIR_OK) return rc;
+    }
+    return TIR_OK;
+}
+
+// Decode forward on the constant one-token-per-sequence layout, through a
+// CUDA graph captured on first use: the launch sequence depends only on the
+// batch's buffers, and every kernel reads positions and pages from the device.
 tir_status decode_forward(tir_batch* b) {
     if (!b->decode_graph) {
         cudaGraph_t g = nullptr;
         cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return bfail(e, "decode graph capture");
-        const int len0 = b->len;
-        const tir_status rc = forward(b, 1);
-        b->len = len0;  // the capture ran nothing
+        const tir_status rc = forward(b, b->uni, b->B, 1);
         e = cudaStreamEndCapture(b->stream, &g);
         if (rc != TIR_OK) {
             if (g) cudaGraphDestroy(g);
@@ -629,15 +729,57 @@ tir_status decode_forward(tir_batch* b) {
     }
     const cudaError_t e = cudaGraphLaunch(b->decode_graph, b->stream);
     if (e != cudaSuccess) return bfail(e, "decode graph launch");
-    b->len += 1;
+    for (int32_t& l : b->h_len) l += 1;
     return TIR_OK;
 }
 
-// Empty every sequence (host and device lengths).
-tir_status reset_len(tir_batch* b) {
-    b->len = 0;
-    const cudaError_t e = cudaMemsetAsync(b->len_dev, 0, 4, b->stream);
-    return e == cudaSuccess ? TIR_OK : bfail(e, "length reset");
+// Validates and lays out a step with counts[s] new tokens of sequence s
+// (ids in sequence order), takes the pages it needs and uploads the layout,
+// the page table and the ids.  *T = rows, *max_cnt = the largest count.
+tir_status stage_step(tir_batch* b, const int32_t* ids_host, const int32_t* counts, int64_t* T, int* max_cnt) {
+    int64_t rows = 0;
+    int mc = 0;
+    for (int s = 0; s < b->B; ++s) {
+        const int c = counts[s];
+        if (c < 0 || c > b->max_tps)
+            return fail(TIR_ERR_INVALID_ARG, "a sequence's token count must be in [0, " + std::to_string(b->max_tps) +
+                                                 "]");
+        if (b->h_len[static_cast<size_t>(s)] + c > b->max_ctx)
+            return fail(TIR_ERR_CTX_OVERFLOW, "sequence " + std::to_string(s) + " would exceed the batch context");
+        rows += c;
+        mc = std::max(mc, c);
+    }
+    // pages: all or nothing
+    size_t need = 0;
+    for (int s = 0; s < b->B; ++s) {
+        const size_t want = static_cast<size_t>((b->h_len[static_cast<size_t>(s)] + counts[s] + kPage - 1) / kPage);
+        need += want > b->seq_pages[static_cast<size_t>(s)].size() ? want - b->seq_pages[static_cast<size_t>(s)].size()
+                                                                  : 0;
+    }
+    if (need > b->free_pages.size()) return fail(TIR_ERR_OOM, "the batch's KV page pool is exhausted");
+    for (int s = 0; s < b->B; ++s) {
+        const tir_status rc = ensure_pages(b, s, b->h_len[static_cast<size_t>(s)] + counts[s]);
+        if (rc != TIR_OK) return rc;
+    }
+    int32_t* row0 = b->h_dyn;
+    int32_t* cnt = b->h_dyn + b->B;
+    int32_t* row_seq = b->h_dyn + 2 * b->B;
+    int64_t r = 0;
+    for (int s = 0; s < b->B; ++s) {
+        row0[s] = static_cast<int32_t>(r);
+        cnt[s] = counts[s];
+        for (int i = 0; i < counts[s]; ++i) row_seq[r++] = s;
+    }
+    cudaError_t e = cudaMemcpyAsync(b->dyn, b->h_dyn, static_cast<size_t>(2 * b->B + rows) * 4,
+                                    cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess && rows > 0)
+        e = cudaMemcpyAsync(b->ids, ids_host, static_cast<size_t>(rows) * 4, cudaMemcpyHostToDevice, b->stream);
+    if (e != cudaSuccess) return bfail(e, "step upload");
+    const tir_status rc = upload_table(b);
+    if (rc != TIR_OK) return rc;
+    *T = rows;
+    *max_cnt = mc;
+    return TIR_OK;
 }
 
 tir_status check_err(tir_batch* b) {
@@ -646,13 +788,12 @@ tir_status check_err(tir_batch* b) {
     if (e != cudaSuccess) return bfail(e, "batched forward");
     const uint32_t code = *b->h_err;
     if (code == 0) return TIR_OK;
-    // reset: sequences and the error word
-    b->len = 0;
+    // reset: every sequence and the error word
     *b->h_err = 0;
     e = cudaMemsetAsync(b->err, 0, 16, b->stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(b->len_dev, 0, 4, b->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return bfail(e, "batch reset");
+    const tir_status rc = reset_all(b);
+    if (rc != TIR_OK) return rc;
     if (code == kBErrBadToken) return fail(TIR_ERR_BAD_TOKEN, "a token id is not in the vocab; the batch was reset");
     return fail(TIR_ERR_TIMEOUT, "device wait timed out; the batch was reset");
 }
@@ -661,14 +802,15 @@ tir_status check_err(tir_batch* b) {
 
 extern "C" {
 
-tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32_t max_tokens_per_seq,
-                            tir_batch** out) {
+tir_status tir_batch_create_paged(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32_t max_tokens_per_seq,
+                                  int32_t n_pages, tir_batch** out) {
     clear_error();
     if (!m || !out) return fail(TIR_ERR_INVALID_ARG, "null argument");
     *out = nullptr;
     const tir_transformer& t = m->t;
-    if (n_seqs <= 0 || max_ctx <= 0 || max_tokens_per_seq <= 0 || max_tokens_per_seq > max_ctx)
-        return fail(TIR_ERR_INVALID_ARG, "need n_seqs, max_ctx > 0 and 0 < max_tokens_per_seq <= max_ctx");
+    if (n_seqs <= 0 || max_ctx <= 0 || max_tokens_per_seq <= 0 || max_tokens_per_seq > max_ctx || n_pages <= 0)
+        return fail(TIR_ERR_INVALID_ARG,
+                    "need n_seqs, max_ctx, n_pages > 0 and 0 < max_tokens_per_seq <= max_ctx");
     if (t.embed_dim % 64 != 0 || t.ffn_dim % 64 != 0 || t.q_heads / t.k_v_heads > 16)
         return fail(TIR_ERR_UNSUPPORTED_SHAPE, "batched path needs embedding and FFN sizes that are multiples of 64 "
                                                "and at most 16 query heads per KV head");
@@ -678,6 +820,11 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
     b->B = n_seqs;
     b->max_ctx = max_ctx;
     b->max_tps = max_tokens_per_seq;
+    b->max_pages = (max_ctx + kPage - 1) / kPage;
+    b->n_pages = n_pages;
+    b->h_len.assign(static_cast<size_t>(n_seqs), 0);
+    b->seq_pages.assign(static_cast<size_t>(n_seqs), {});
+    for (int32_t p = n_pages - 1; p >= 0; --p) b->free_pages.push_back(p);  // page 0 handed out first
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
     b->sms = sms > 0 ? sms : 148;
@@ -688,15 +835,13 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
     const int64_t H = t.embed_dim, KVD = t.kv_dim, F = t.ffn_dim, V = t.vocab, L = t.layers;
     const int64_t T = static_cast<int64_t>(n_seqs) * max_tokens_per_seq;
     const int64_t kmax = std::max(H, F);
-    const size_t cache = static_cast<size_t>(L) * n_seqs * max_ctx * KVD;
-    // Rows of partial tiles a matmul of n x k leaves over the token counts the
-    // batch runs (n_seqs x tokens_per_seq): split-K count x tokens, at most.
+    const size_t cache = static_cast<size_t>(L) * n_pages * kPage * KVD;
+    // Rows of partial tiles a matmul of n x k leaves over every row count a
+    // step can have (1 .. n_seqs x tokens_per_seq): split-K count x rows, at most.
     auto part_rows = [&](int64_t n, int64_t k) {
         size_t rows = 0;
-        for (int64_t tps = 1; tps <= max_tokens_per_seq; ++tps) {
-            const int64_t tok = static_cast<int64_t>(n_seqs) * tps;
+        for (int64_t tok = 1; tok <= T; ++tok)
             rows = std::max(rows, static_cast<size_t>(gemm_real_splits(k, gemm_splits(n, k, tok, b->sms)) * tok));
-        }
         return rows;
     };
     bool ok = balloc(b, cache * 4, &b->kc) && balloc(b, cache * 4, &b->vc) &&
@@ -707,23 +852,36 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
               balloc(b, part_rows(2 * F, H) * 2 * F * 4, &b->GU) &&
               balloc(b, static_cast<size_t>(gemm_real_splits(H, gemm_splits(V, H, n_seqs, b->sms))) * n_seqs * V * 4,
                      &b->LG) &&
-              balloc(b, 16, &b->len_dev) &&
+              balloc(b, static_cast<size_t>(n_seqs) * 4, &b->seq_len) &&
+              balloc(b, static_cast<size_t>(n_seqs) * b->max_pages * 4, &b->table) &&
+              balloc(b, static_cast<size_t>(2 * n_seqs + T) * 4, &b->dyn) &&
+              balloc(b, static_cast<size_t>(3 * n_seqs) * 4, &b->uni) &&
               balloc(b, static_cast<size_t>(gemm_x_plane_bytes(T, kmax)), &b->planes) &&
-              balloc(b, static_cast<size_t>(gemm_tokens_padded(T)) * 4, &b->inv) &&
-              balloc(b, T * 4, &b->ids) &&
+              balloc(b, static_cast<size_t>(gemm_tokens_padded(T)) * 4, &b->inv) && balloc(b, T * 4, &b->ids) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->rows) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->next) && balloc(b, 16, &b->err);
     if (!ok || cudaMallocHost(&b->h_next, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
-        cudaMallocHost(&b->h_err, 16) != cudaSuccess) {
+        cudaMallocHost(&b->h_err, 16) != cudaSuccess ||
+        cudaMallocHost(&b->h_table, static_cast<size_t>(n_seqs) * b->max_pages * 4) != cudaSuccess ||
+        cudaMallocHost(&b->h_dyn, static_cast<size_t>(2 * n_seqs + T) * 4) != cudaSuccess) {
         delete b;
         return fail(TIR_ERR_OOM, "batch allocation failed");
     }
-    std::vector<float> c, s;
-    rope_table(t.base_freq, kHeadDim, max_ctx, c, s);
+    std::memset(b->h_table, 0, static_cast<size_t>(n_seqs) * b->max_pages * 4);
+    std::vector<int32_t> uni(static_cast<size_t>(3 * n_seqs));
+    for (int s_ = 0; s_ < n_seqs; ++s_) {
+        uni[static_cast<size_t>(s_)] = s_;           // row0
+        uni[static_cast<size_t>(n_seqs + s_)] = 1;   // cnt
+        uni[static_cast<size_t>(2 * n_seqs + s_)] = s_;  // row_seq
+    }
+    std::vector<float> c, sn;
+    rope_table(t.base_freq, kHeadDim, max_ctx, c, sn);
     if (cudaMemcpy(b->rcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(b->rsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(b->err, 0, 16) != cudaSuccess ||
-        cudaMemset(b->len_dev, 0, 16) != cudaSuccess || gemm_configure() != 0) {
+        cudaMemcpy(b->rsin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(b->uni, uni.data(), uni.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(b->table, 0, static_cast<size_t>(n_seqs) * b->max_pages * 4) != cudaSuccess ||
+        cudaMemset(b->err, 0, 16) != cudaSuccess || cudaMemset(b->seq_len, 0, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
+        gemm_configure() != 0) {
         delete b;
         return fail(TIR_ERR_CUDA, "batch initialisation failed");
     }
@@ -756,29 +914,101 @@ tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32
     return TIR_OK;
 }
 
+tir_status tir_batch_create(tir_model* m, int32_t n_seqs, int32_t max_ctx, int32_t max_tokens_per_seq,
+                            tir_batch** out) {
+    if (n_seqs <= 0 || max_ctx <= 0) {
+        clear_error();
+        return fail(TIR_ERR_INVALID_ARG, "need n_seqs, max_ctx > 0 and 0 < max_tokens_per_seq <= max_ctx");
+    }
+    return tir_batch_create_paged(m, n_seqs, max_ctx, max_tokens_per_seq, n_seqs * ((max_ctx + kPage - 1) / kPage),
+                                  out);
+}
+
 void tir_batch_destroy(tir_batch* b) { delete b; }
 
 tir_status tir_batch_reset(tir_batch* b) {
+    clear_error();
     if (!b) return fail(TIR_ERR_INVALID_ARG, "null argument");
     cudaSetDevice(b->m->device);
-    return reset_len(b);
+    return reset_all(b);
 }
 
-int32_t tir_batch_len(const tir_batch* b) { return b ? b->len : 0; }
+tir_status tir_batch_reset_seq(tir_batch* b, int32_t seq) {
+    clear_error();
+    if (!b || seq < 0 || seq >= b->B) return fail(TIR_ERR_INVALID_ARG, "null batch or sequence out of range");
+    cudaSetDevice(b->m->device);
+    const cudaError_t e = cudaStreamSynchronize(b->stream);  // its pages may still be read
+    if (e != cudaSuccess) return bfail(e, "sequence reset");
+    return release_seq(b, seq);
+}
+
+int32_t tir_batch_len(const tir_batch* b) {
+    if (!b) return 0;
+    int32_t mx = 0;
+    for (int32_t l : b->h_len) mx = std::max(mx, l);
+    return mx;
+}
+
+int32_t tir_batch_seq_len(const tir_batch* b, int32_t seq) {
+    return b && seq >= 0 && seq < b->B ? b->h_len[static_cast<size_t>(seq)] : 0;
+}
+
+int32_t tir_batch_free_pages(const tir_batch* b) { return b ? static_cast<int32_t>(b->free_pages.size()) : 0; }
 
 void* tir_batch_stream(tir_batch* b) { return b ? static_cast<void*>(b->stream) : nullptr; }
+
+tir_status tir_batch_step_ragged(tir_batch* b, const int32_t* ids_host, const int32_t* counts_host,
+                                 int32_t* next_ids_host) {
+    clear_error();
+    if (!b || !counts_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    int64_t total = 0;
+    for (int s_ = 0; s_ < b->B; ++s_) total += counts_host[s_] > 0 ? counts_host[s_] : 0;
+    if (total > 0 && !ids_host) return fail(TIR_ERR_INVALID_ARG, "null ids");
+    cudaSetDevice(b->m->device);
+    int64_t T = 0;
+    int max_cnt = 0;
+    tir_status rc = stage_step(b, ids_host, counts_host, &T, &max_cnt);
+    if (rc != TIR_OK) return rc;
+    if (T == 0) return TIR_OK;
+    rc = forward(b, b->dyn, T, max_cnt);
+    if (rc != TIR_OK) return rc;
+    if (next_ids_host) {
+        const cudaError_t e =
+            cudaMemcpyAsync(b->h_next, b->next, static_cast<size_t>(b->B) * 4, cudaMemcpyDeviceToHost, b->stream);
+        if (e != cudaSuccess) return bfail(e, "id readback");
+    }
+    rc = check_err(b);
+    if (rc != TIR_OK) return rc;
+    for (int s_ = 0; s_ < b->B; ++s_) b->h_len[static_cast<size_t>(s_)] += counts_host[s_];
+    if (next_ids_host) std::copy(b->h_next, b->h_next + b->B, next_ids_host);
+    return TIR_OK;
+}
 
 tir_status tir_batch_step(tir_batch* b, const int32_t* ids_host, int32_t tokens_per_seq, int32_t* next_ids_host) {
     clear_error();
     if (!b || !ids_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
     if (tokens_per_seq <= 0 || tokens_per_seq > b->max_tps)
         return fail(TIR_ERR_INVALID_ARG, "tokens_per_seq must be in [1, " + std::to_string(b->max_tps) + "]");
-    if (b->len + tokens_per_seq > b->max_ctx) return fail(TIR_ERR_CTX_OVERFLOW, "batch context is full");
+    const std::vector<int32_t> counts(static_cast<size_t>(b->B), tokens_per_seq);
+    if (tokens_per_seq > 1) return tir_batch_step_ragged(b, ids_host, counts.data(), next_ids_host);
+    // one token each: the captured decode forward on the constant layout
     cudaSetDevice(b->m->device);
-    const size_t n = static_cast<size_t>(b->B) * tokens_per_seq;
-    cudaError_t e = cudaMemcpyAsync(b->ids, ids_host, n * 4, cudaMemcpyHostToDevice, b->stream);
+    for (int s_ = 0; s_ < b->B; ++s_)
+        if (b->h_len[static_cast<size_t>(s_)] + 1 > b->max_ctx)
+            return fail(TIR_ERR_CTX_OVERFLOW, "sequence " + std::to_string(s_) + " would exceed the batch context");
+    size_t need = 0;
+    for (int s_ = 0; s_ < b->B; ++s_) {
+        const size_t want = static_cast<size_t>((b->h_len[static_cast<size_t>(s_)] + 1 + kPage - 1) / kPage);
+        need += want > b->seq_pages[static_cast<size_t>(s_)].size() ? 1 : 0;
+    }
+    if (need > b->free_pages.size()) return fail(TIR_ERR_OOM, "the batch's KV page pool is exhausted");
+    tir_status rc = TIR_OK;
+    for (int s_ = 0; s_ < b->B && rc == TIR_OK; ++s_) rc = ensure_pages(b, s_, b->h_len[static_cast<size_t>(s_)] + 1);
+    if (rc == TIR_OK) rc = upload_table(b);
+    if (rc != TIR_OK) return rc;
+    cudaError_t e = cudaMemcpyAsync(b->ids, ids_host, static_cast<size_t>(b->B) * 4, cudaMemcpyHostToDevice, b->stream);
     if (e != cudaSuccess) return bfail(e, "id upload");
-    tir_status rc = tokens_per_seq == 1 ? decode_forward(b) : forward(b, tokens_per_seq);
+    rc = decode_forward(b);
     if (rc != TIR_OK) return rc;
     if (next_ids_host) {
         e = cudaMemcpyAsync(b->h_next, b->next, static_cast<size_t>(b->B) * 4, cudaMemcpyDeviceToHost, b->stream);
@@ -790,7 +1020,8 @@ tir_status tir_batch_step(tir_batch* b, const int32_t* ids_host, int32_t tokens_
 }
 
 // Per sequence: prefill n_prompt ids, then cap greedy steps (n_prompt + cap
-// forwards, as generate_capped, src/lib.rs:239-314); out_ids [B][cap].
+// forwards, as generate_capped, src/lib.rs:239-314); out_ids [B][cap].  Every
+// sequence starts empty; the pages for the whole generation are taken first.
 tir_status tir_batch_generate(tir_batch* b, const int32_t* prompts_host, int32_t n_prompt, int32_t cap,
                               int32_t* out_ids_host) {
     clear_error();
@@ -799,11 +1030,13 @@ tir_status tir_batch_generate(tir_batch* b, const int32_t* prompts_host, int32_t
         return fail(TIR_ERR_INVALID_ARG, "n_prompt must be in [1, " + std::to_string(b->max_tps) + "], cap >= 0");
     if (n_prompt + cap > b->max_ctx) return fail(TIR_ERR_CTX_OVERFLOW, "prompt + cap exceeds the batch context");
     cudaSetDevice(b->m->device);
-    tir_status rc = reset_len(b);
+    tir_status rc = reset_all(b);
     if (rc != TIR_OK) return rc;
-    const size_t n = static_cast<size_t>(b->B) * n_prompt;
-    cudaError_t e = cudaMemcpyAsync(b->ids, prompts_host, n * 4, cudaMemcpyHostToDevice, b->stream);
-    if (e != cudaSuccess) return bfail(e, "prompt upload");
+    const size_t per = static_cast<size_t>((n_prompt + cap + kPage - 1) / kPage);
+    if (per * static_cast<size_t>(b->B) > b->free_pages.size())
+        return fail(TIR_ERR_OOM, "the batch's KV page pool is too small for prompt + cap on every sequence");
+    for (int s_ = 0; s_ < b->B && rc == TIR_OK; ++s_) rc = ensure_pages(b, s_, n_prompt + cap);
+    if (rc != TIR_OK) return rc;
     if (cap > b->gen_cap) {  // generated ids [cap][B] on the device
         cudaStreamSynchronize(b->stream);
         if (b->gen) cudaFree(b->gen);
@@ -813,7 +1046,13 @@ tir_status tir_batch_generate(tir_batch* b, const int32_t* prompts_host, int32_t
             return fail(TIR_ERR_OOM, "output allocation failed");
         b->gen_cap = cap;
     }
-    rc = forward(b, n_prompt);
+    const std::vector<int32_t> counts(static_cast<size_t>(b->B), n_prompt);
+    int64_t T = 0;
+    int max_cnt = 0;
+    rc = stage_step(b, prompts_host, counts.data(), &T, &max_cnt);  // uploads the page table too
+    if (rc == TIR_OK) rc = forward(b, b->dyn, T, max_cnt);
+    if (rc == TIR_OK)
+        for (int32_t& l : b->h_len) l += n_prompt;
     const unsigned fb = static_cast<unsigned>((b->B + 255) / 256);
     for (int i = 0; rc == TIR_OK && i < cap; ++i) {
         feed_kernel<<<fb, 256, 0, b->stream>>>(b->next, b->ids, b->gen + static_cast<size_t>(i) * b->B, b->B);
@@ -821,14 +1060,15 @@ tir_status tir_batch_generate(tir_batch* b, const int32_t* prompts_host, int32_t
     }
     std::vector<int32_t> host(static_cast<size_t>(cap) * b->B);
     if (rc == TIR_OK && cap > 0) {
-        e = cudaMemcpyAsync(host.data(), b->gen, host.size() * 4, cudaMemcpyDeviceToHost, b->stream);
+        const cudaError_t e = cudaMemcpyAsync(host.data(), b->gen, host.size() * 4, cudaMemcpyDeviceToHost, b->stream);
         if (e != cudaSuccess) rc = bfail(e, "id readback");
     }
     const tir_status rc2 = check_err(b);
     if (rc == TIR_OK) rc = rc2;
     if (rc == TIR_OK)
-        for (int s = 0; s < b->B; ++s)
-            for (int i = 0; i < cap; ++i) out_ids_host[static_cast<size_t>(s) * cap + i] = host[static_cast<size_t>(i) * b->B + s];
+        for (int s_ = 0; s_ < b->B; ++s_)
+            for (int i = 0; i < cap; ++i)
+                out_ids_host[static_cast<size_t>(s_) * cap + i] = host[static_cast<size_t>(i) * b->B + s_];
     return rc;
 }
 

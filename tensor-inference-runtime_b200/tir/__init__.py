@@ -127,6 +127,11 @@ SIGNATURES = {
     "tir_swiglu": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_swiglu_static": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_batch_create": (C.c_int, [_vp, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_vp)]),
+    "tir_batch_create_paged": (C.c_int, [_vp, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.POINTER(_vp)]),
+    "tir_batch_reset_seq": (C.c_int, [_vp, C.c_int32]),
+    "tir_batch_seq_len": (C.c_int32, [_vp, C.c_int32]),
+    "tir_batch_free_pages": (C.c_int32, [_vp]),
+    "tir_batch_step_ragged": (C.c_int, [_vp, _vp, _vp, _vp]),
     "tir_batch_destroy": (None, [_vp]),
     "tir_batch_reset": (C.c_int, [_vp]),
     "tir_batch_len": (C.c_int32, [_vp]),
@@ -539,13 +544,18 @@ def q8_matmul_qact(x, quants, scales, out, n, k, stream=None):
 
 
 class Batch:
-    """n_seqs sequences decoded in lockstep on the tensor-core path."""
+    """n_seqs sequences on the tensor-core path with a paged KV cache (pool of
+    n_pages pages of 16 positions; default: every sequence can reach max_ctx)."""
 
-    def __init__(self, model, n_seqs, max_ctx, max_tokens_per_seq):
+    def __init__(self, model, n_seqs, max_ctx, max_tokens_per_seq, n_pages=None):
         self.model = model
         self.n_seqs = n_seqs
         h = C.c_void_p()
-        check(lib().tir_batch_create(model.handle, n_seqs, max_ctx, max_tokens_per_seq, C.byref(h)))
+        if n_pages is None:
+            check(lib().tir_batch_create(model.handle, n_seqs, max_ctx, max_tokens_per_seq, C.byref(h)))
+        else:
+            check(lib().tir_batch_create_paged(model.handle, n_seqs, max_ctx, max_tokens_per_seq, n_pages,
+                                               C.byref(h)))
         self._h = h
         self._destroy = lib().tir_batch_destroy  # held by the object: usable at interpreter teardown
 
@@ -564,6 +574,26 @@ class Batch:
 
     def reset(self):
         check(lib().tir_batch_reset(self._h))
+
+    def reset_seq(self, seq):
+        check(lib().tir_batch_reset_seq(self._h, seq))
+
+    def seq_len(self, seq):
+        return lib().tir_batch_seq_len(self._h, seq)
+
+    def free_pages(self):
+        return lib().tir_batch_free_pages(self._h)
+
+    def step_ragged(self, ids_per_seq):
+        """ids_per_seq: one id sequence per batch sequence (empty: idle) ->
+        greedy next id per sequence (meaningless for idle ones)."""
+        counts = np.array([len(x) for x in ids_per_seq], np.int32)
+        assert counts.size == self.n_seqs
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(x, np.int32).reshape(-1) for x in ids_per_seq])
+                                    if counts.sum() else np.zeros(1, np.int32), np.int32)
+        out = np.zeros(self.n_seqs, np.int32)
+        check(lib().tir_batch_step_ragged(self._h, flat.ctypes.data, counts.ctypes.data, out.ctypes.data))
+        return out
 
     def __len__(self):
         return lib().tir_batch_len(self._h)

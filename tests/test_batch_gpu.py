@@ -65,3 +65,79 @@ def test_batch_errors(tirlib, tiny):
     nxt = b.step(nxt[:, None])
     assert len(b) == 2
     b.close()
+
+
+def _oracle_tokens(orc, om, ids, cap):
+    """Greedy continuation of `ids` on the oracle, with top-2 margins."""
+    return oracle_greedy(orc, om, np.asarray(ids, np.int32), cap)
+
+
+def test_ragged_steps_match_each_sequence(tirlib, orc, tiny):
+    """Sequences of different prompt lengths, fed in chunks and decoded in
+    mixed steps (some prefilling, some decoding, some idle); every sequence
+    must still decode what the oracle decodes for it alone."""
+    m, om = tiny
+    vocab = m.info["vocab"]
+    prompts = [synth.prompt_ids(n, vocab, seed=300 + n) for n in (3, 17, 9)]
+    b = tirlib.Batch(m, 3, max_ctx=64, max_tokens_per_seq=8)
+    got = [[], [], []]
+    fed = [0, 0, 0]
+    pending = [None, None, None]
+    for _ in range(14):
+        chunk = []
+        for s_ in range(3):
+            if fed[s_] < len(prompts[s_]):
+                n = min(8, len(prompts[s_]) - fed[s_], 1 + (s_ + fed[s_]) % 5)  # uneven prompt chunks
+                chunk.append(prompts[s_][fed[s_]:fed[s_] + n])
+                fed[s_] += n
+            elif len(got[s_]) < 6 and pending[s_] is not None and (s_ != 2 or len(got[2]) < 3 or _ % 2 == 0):
+                chunk.append([pending[s_]])  # decode (sequence 2 idles every other step late on)
+                got[s_].append(pending[s_])
+            else:
+                chunk.append([])
+        nxt = b.step_ragged(chunk)
+        for s_ in range(3):
+            if len(chunk[s_]) > 0:
+                pending[s_] = int(nxt[s_])
+    for s_ in range(3):
+        assert b.seq_len(s_) == len(prompts[s_]) + len(got[s_])
+        ref, margins, _ = _oracle_tokens(orc, om, prompts[s_], len(got[s_]))
+        compare_tokens(np.array(got[s_], np.int32), ref, margins)
+    b.close()
+
+
+def test_continuous_batching_reuses_pages(tirlib, orc, tiny):
+    """A finished sequence is reset and its slot starts a new prompt while the
+    other keeps decoding; pages go back to the pool and are reused."""
+    m, om = tiny
+    vocab = m.info["vocab"]
+    b = tirlib.Batch(m, 2, max_ctx=48, max_tokens_per_seq=16, n_pages=4)
+    assert b.free_pages() == 4
+    p0, p1, p2 = (synth.prompt_ids(n, vocab, seed=400 + n) for n in (14, 5, 7))
+    nxt = b.step_ragged([p0, p1])
+    out0, out1 = [int(nxt[0])], [int(nxt[1])]
+    for _ in range(4):
+        nxt = b.step_ragged([[out0[-1]], [out1[-1]]])
+        out0.append(int(nxt[0]))
+        out1.append(int(nxt[1]))
+    assert 4 - b.free_pages() == 2 + 1  # 18 positions -> 2 pages, 9 -> 1 page
+    b.reset_seq(1)
+    assert b.free_pages() == 4 - 2 and b.seq_len(1) == 0
+    nxt = b.step_ragged([[out0[-1]], p2])  # slot 1 restarts with a new prompt
+    out0.append(int(nxt[0]))
+    out2 = [int(nxt[1])]
+    for _ in range(3):
+        nxt = b.step_ragged([[out0[-1]], [out2[-1]]])
+        out0.append(int(nxt[0]))
+        out2.append(int(nxt[1]))
+    for prompt, out in ((p0, out0), (p1, out1), (p2, out2)):
+        ref, margins, _ = _oracle_tokens(orc, om, prompt, len(out))
+        compare_tokens(np.array(out, np.int32), ref, margins)
+    # one free page left: a step needing two more does not fit, and nothing changes
+    assert b.free_pages() == 1
+    with pytest.raises(tirlib.TirError) as e:
+        b.step_ragged([synth.prompt_ids(16, vocab, seed=8), synth.prompt_ids(16, vocab, seed=9)])
+    assert e.value.name == "OOM"
+    assert b.seq_len(0) == len(p0) + len(out0) - 1 and b.seq_len(1) == len(p2) + len(out2) - 1
+    assert b.free_pages() == 1
+    b.close()
