@@ -714,11 +714,14 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const PhaseDesc&
 // units, and issues the copies kWarpSlots tiles ahead into the freed slots; the per-thread
 // partials are reduced over each warp (reduce8) into s.part, and after one CTA
 // barrier thread e runs the epilogue of batch row e, summing the partials of
-// the row lane's warps in order (deterministic).
+// the row lane's warps in order (deterministic).  The last batch's copies are
+// left to the caller (`deferred` of them), which issues them after the phase
+// is released: issuing copies occupies a warp ~1k cycles per tile, which would
+// otherwise delay the release that every CTA waits for.
 template <int M>
 __device__ __forceinline__ bool gemv_tiles(const DecodeParams& p, Smem& s, Stream& sw, const PhaseDesc& d,
                                            const StepCtx& st, int ph, uint32_t gidx, const Prefetch& pf,
-                                           TraceAcc& tr, unsigned long long& best) {
+                                           TraceAcc& tr, unsigned long long& best, int& deferred) {
     static_assert(M == kTileMult, "tiles hold kTileMult rows per row lane");
     constexpr int TB = 8 / M;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -779,9 +782,13 @@ __device__ __forceinline__ bool gemv_tiles(const DecodeParams& p, Smem& s, Strea
             }
         }
         __syncwarp();  // the batch's slots are free
-        // 3. refill them, kWarpSlots tiles ahead
-        for (int ti = 0; ti < nt; ++ti)
-            stream_next(p, s, sw, gidx + static_cast<uint32_t>(k0 + ti + kWarpSlots), warp, lane);
+        // 3. refill them, kWarpSlots tiles ahead (the last batch's: after the release)
+        if (k0 + TB < nm) {
+            for (int ti = 0; ti < nt; ++ti)
+                stream_next(p, s, sw, gidx + static_cast<uint32_t>(k0 + ti + kWarpSlots), warp, lane);
+        } else {
+            deferred = nt;
+        }
         if (tr.on) tr.tiles += static_cast<unsigned long long>(nt);
         const float y8 = reduce8(t, lane);
         if (warp_on && (lane & 3) == 0) s.part[buf][warp][lane >> 2] = y8;
@@ -813,7 +820,7 @@ __device__ __forceinline__ bool gemv_tiles(const DecodeParams& p, Smem& s, Strea
 template <bool QACT>
 __device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, Stream& sw, const PhaseDesc& d,
                                            const StepCtx& st, int ph, uint32_t gidx, const Prefetch& pf,
-                                           TraceAcc& tr) {
+                                           TraceAcc& tr, int& deferred) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nm = s.nmine[ph];
     if (nm == 0) {
@@ -827,7 +834,7 @@ __device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, Strea
     trace_mark(p, ph, st.f, 2);
     unsigned long long best = 0ull;
     bool ok;
-    ok = gemv_tiles<kTileMult>(p, s, sw, d, st, ph, gidx, pf, tr, best);
+    ok = gemv_tiles<kTileMult>(p, s, sw, d, st, ph, gidx, pf, tr, best, deferred);
     if (d.epi == EPI_LOGITS) {
 #pragma unroll
         for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(FULL, best, o));
@@ -1070,6 +1077,7 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
             }
             trace_mark(p, ph, f, 1);
             bool ok = true;
+            int deferred = 0;  // weight copies of the phase's last batch, issued after the release
             if (d.kind == PH_ATTN) {
                 ok = attention_phase(p, s, d, st, abar_phase, prefetched);
             } else {
@@ -1077,7 +1085,7 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
                     st.token = s.token;
                     st.x0_given = (f == 0 && p.x0 != nullptr);
                 }
-                ok = gemv_phase<QACT>(p, s, sw, d, st, ph, gidx, pf, tr);
+                ok = gemv_phase<QACT>(p, s, sw, d, st, ph, gidx, pf, tr, deferred);
                 gidx += static_cast<uint32_t>(s.nmine[ph]);
             }
             if (!ok) s.abort_flag = 1;  // any warp: the CTA stops after this phase
@@ -1106,6 +1114,12 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
                 }
             }
             trace_mark(p, ph, f, 3);
+            // 3. the deferred copies of the phase's last batch
+            {
+                const int warp = tid >> 5, lane = tid & 31;
+                for (int ti = 0; ti < deferred; ++ti)
+                    stream_next(p, s, sw, gidx - static_cast<uint32_t>(deferred - ti) + kWarpSlots, warp, lane);
+            }
         }
     }
 }
