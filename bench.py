@@ -126,6 +126,11 @@ class ClockSampler:
             self.thread.start()
         except OSError:
             self.proc = None
+        # nvidia-smi's start-up can hold the driver for seconds: the timed
+        # region opens only once it delivers samples (at most 10 s)
+        t0 = time.perf_counter()
+        while self.proc and not self.rows and self.proc.poll() is None and time.perf_counter() - t0 < 10.0:
+            time.sleep(0.01)
         return self
 
     def _read(self):
