@@ -185,6 +185,12 @@ tir_status tir_forward(tir_state *s, int32_t token_id, int32_t pos, float *logit
  * empty cache.  last_logits_host (optional): logits of the final forward. */
 tir_status tir_generate_capped(tir_state *s, const int32_t *prompt_host, int32_t n_prompt,
                                int32_t cap, int32_t *out_ids_host, float *last_logits_host);
+/* The prompt pass of generate_capped alone: seq_len ids from position 0 of an
+ * empty cache; last_logits_host (optional) gets the last position's logits.
+ * n_seqs must be 1 (a tir_state holds one sequence; n_seqs sequences prefill
+ * with tir_batch_step, tokens_per_seq = seq_len). */
+tir_status tir_prefill(tir_state *s, const int32_t *ids_host, int32_t n_seqs, int32_t seq_len,
+                       float *last_logits_host);
 /* Same with device buffers, asynchronous on tir_state_stream(s). */
 tir_status tir_generate_capped_device(tir_state *s, const int32_t *prompt_dev, int32_t n_prompt,
                                       int32_t cap, int32_t *out_ids_dev);
@@ -199,6 +205,8 @@ tir_status tir_test_forward(tir_state *s, int32_t *out_id);
  * save_intermediate, src/forward.rs:287-308).  Enable before the forward. */
 tir_status tir_state_enable_dump(tir_state *s, int32_t enable);
 tir_status tir_state_dump(tir_state *s, float *out_host);
+/* The layer outputs alone: layers x embed_dim floats (rows 1.. of the dump). */
+tir_status tir_debug_dump_layers(tir_state *s, float *out_host);
 /* Phase timeline (profiling; the reference's tracing is the debug-build
  * save_intermediate, src/forward.rs:287-308): with step >= 0, every later
  * launch records, for forward step `step`, eight values per phase per CTA:
@@ -278,6 +286,10 @@ tir_status tir_batch_step(tir_batch *b, const int32_t *ids_host, int32_t tokens_
  * [n_seqs][cap]. */
 tir_status tir_batch_generate(tir_batch *b, const int32_t *prompts_host, int32_t n_prompt, int32_t cap,
                               int32_t *out_ids_host);
+/* Logits of every sequence's last row in the last forward, logits_host
+ * [n_seqs][vocab] (forward's return value, src/forward.rs:242-252, per
+ * sequence; a sequence idle in that step gets zeros). */
+tir_status tir_batch_logits(tir_batch *b, float *logits_host);
 
 /* ---- op-level kernels (device pointers, asynchronous on `stream`) --------- */
 

@@ -892,6 +892,20 @@ tir_status tir_generate_capped(tir_state* s, const int32_t* prompt_host, int32_t
     return TIR_OK;
 }
 
+// The prompt phase of generate_capped (src/lib.rs:239-314, token by token
+// from position 0) without greedy steps: the state then holds the prompt's
+// KV cache and last_logits_host (optional) the last position's logits.  A
+// tir_state holds one sequence; n_seqs sequences prefill through
+// tir_batch_step (tokens_per_seq = seq_len).
+tir_status tir_prefill(tir_state* s, const int32_t* ids_host, int32_t n_seqs, int32_t seq_len, float* last_logits_host) {
+    clear_error();
+    if (!s) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (n_seqs != 1)
+        return fail(TIR_ERR_INVALID_ARG, "a tir_state holds one sequence: prefill n_seqs sequences with tir_batch_step");
+    if (seq_len <= 0) return fail(TIR_ERR_INVALID_ARG, "seq_len must be positive");
+    return tir_generate_capped(s, ids_host, seq_len, 0, nullptr, last_logits_host);
+}
+
 // generate_capped on text (src/lib.rs:239-314): encode (BOS + BPE ids), the
 // prompt fed token by token, then cap greedy ids.
 tir_status tir_generate_capped_text(tir_state* s, const tir_tokenizer* tk, const char* text, int64_t text_len,
@@ -970,6 +984,22 @@ tir_status tir_state_dump(tir_state* s, float* out_host) {
     CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
     const size_t n = static_cast<size_t>(s->m->t.layers + 1) * s->m->t.embed_dim;
     CUDA_TRY(cudaMemcpyAsync(out_host, s->dump, n * 4, cudaMemcpyDeviceToHost, s->stream), "dump readback");
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "dump readback");
+    return TIR_OK;
+}
+
+// The per-layer outputs [L][H] of the last forward (rows 1..L of the dump),
+// for layer-by-layer comparison with the reference's forward
+// (src/forward.rs:13-258); the dump must be on (tir_state_enable_dump).
+tir_status tir_debug_dump_layers(tir_state* s, float* out_host) {
+    clear_error();
+    if (!s || !out_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (!s->dump_on) return fail(TIR_ERR_INVALID_ARG, "dump not enabled");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    const size_t h = s->m->t.embed_dim;
+    CUDA_TRY(cudaMemcpyAsync(out_host, s->dump + h, static_cast<size_t>(s->m->t.layers) * h * 4, cudaMemcpyDeviceToHost,
+                             s->stream),
+             "dump readback");
     CUDA_TRY(cudaStreamSynchronize(s->stream), "dump readback");
     return TIR_OK;
 }

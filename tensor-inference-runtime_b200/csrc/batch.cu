@@ -429,16 +429,17 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int parts, int64
     }
 }
 
-// Each sequence's last new row (row 0 for an idle sequence, whose logits are
-// not used); then every sequence's device length advances by its new tokens
-// (every kernel of the forward that reads it has run by now).
+// Each sequence's last new row (-1 for an idle sequence: its logits row is
+// zeros, and no live row is gathered twice); then every sequence's device
+// length advances by its new tokens (every kernel of the forward that reads it
+// has run by now).
 __global__ void last_rows_kernel(int32_t* rows, Pages pg, int n_seqs) {
     griddep_launch_dependents();
     griddep_wait();
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s < n_seqs) {
         const int cnt = pg.seq_cnt[s];
-        rows[s] = cnt > 0 ? pg.seq_row0[s] + cnt - 1 : 0;
+        rows[s] = cnt > 0 ? pg.seq_row0[s] + cnt - 1 : -1;
         pg.seq_len[s] += cnt;
     }
 }
@@ -480,6 +481,8 @@ struct tir_batch {
     float *X = nullptr, *Y = nullptr, *QKV = nullptr, *ATT = nullptr, *GU = nullptr, *LG = nullptr, *inv = nullptr;
     uint8_t* planes = nullptr;
     int32_t *ids = nullptr, *rows = nullptr, *next = nullptr, *h_next = nullptr;
+    float* logits = nullptr;  // [B][V] summed lm_head rows (allocated on first tir_batch_logits)
+    int lm_parts = 0;         // partial tiles of the last forward's lm_head output (0: no forward yet)
     uint32_t *err = nullptr, *h_err = nullptr;
     // Sequences and pages.  seq_len lives on the device (kernels read and
     // advance it, so graph replays stay valid); h_len mirrors it.
@@ -501,6 +504,7 @@ struct tir_batch {
         if (stream) cudaStreamSynchronize(stream);
         if (decode_graph) cudaGraphExecDestroy(decode_graph);
         if (gen) cudaFree(gen);
+        if (logits) cudaFree(logits);
         for (void* p : allocs) cudaFree(p);
         if (h_next) cudaFreeHost(h_next);
         if (h_err) cudaFreeHost(h_err);
@@ -650,6 +654,7 @@ tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
                                                 b->planes, b->inv, st, true))) != TIR_OK)
         return rc;
     if ((rc = mm(b, b->B, b->lm, b->LG, &parts)) != TIR_OK) return rc;
+    b->lm_parts = parts;
     launch_kernel(argmax_rows_kernel, dim3(static_cast<unsigned>(b->B)), dim3(256), 0, st, true, b->LG, parts,
                   static_cast<int64_t>(b->B) * V, static_cast<int64_t>(V), b->next);
     cudaError_t e = cudaGetLastError();
@@ -1017,6 +1022,24 @@ tir_status tir_batch_step(tir_batch* b, const int32_t* ids_host, int32_t tokens_
     rc = check_err(b);
     if (rc == TIR_OK && next_ids_host) std::copy(b->h_next, b->h_next + b->B, next_ids_host);
     return rc;
+}
+
+// Logits [n_seqs][vocab] of every sequence's last row in the last forward
+// (what src/forward.rs:242-252 returns per sequence; a sequence that took no
+// token in that step gets zeros): the lm_head partial tiles summed in order.
+tir_status tir_batch_logits(tir_batch* b, float* logits_host) {
+    clear_error();
+    if (!b || !logits_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (b->lm_parts == 0) return fail(TIR_ERR_INVALID_ARG, "no forward has run on this batch");
+    cudaSetDevice(b->m->device);
+    const int64_t n = static_cast<int64_t>(b->B) * static_cast<int64_t>(b->m->t.vocab);
+    if (!b->logits && cudaMalloc(reinterpret_cast<void**>(&b->logits), static_cast<size_t>(n) * 4) != cudaSuccess)
+        return fail(TIR_ERR_OOM, "logits allocation failed");
+    int e = launch_gemm_sum_parts(b->LG, b->lm_parts, n, n, b->logits, b->stream, false);
+    if (e != 0) return bfail(static_cast<cudaError_t>(e), "logits sum");
+    cudaError_t ce = cudaMemcpyAsync(logits_host, b->logits, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, b->stream);
+    if (ce != cudaSuccess) return bfail(ce, "logits readback");
+    return check_err(b);
 }
 
 // Per sequence: prefill n_prompt ids, then cap greedy steps (n_prompt + cap

@@ -449,7 +449,9 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_x_planes_kernel(const floa
 // multiplication by the correctly rounded reciprocal), h = row
 // rows ? rows[t] : t of X -- after X += Y on that row when Y is given (the
 // residual add of src/forward.rs, fused here so the matmul before it only
-// stores), Y the sum of y_parts partial tiles y_part floats apart.
+// stores), Y the sum of y_parts partial tiles y_part floats apart.  Gathered
+// row indices must be distinct (each row's tile 0 takes its sum in place);
+// rows[t] < 0 marks an unused slot (zero planes).
 __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* __restrict__ X,
                                                                          float* __restrict__ Y, int y_parts,
                                                                          int64_t y_part,
@@ -462,8 +464,10 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* 
     griddep_launch_dependents();
     griddep_wait();
     const int64_t t = blockIdx.x;
-    const bool live = t < tokens;
-    const int64_t xr = live ? (rows ? static_cast<int64_t>(rows[t]) : t) : 0;
+    // a gathered row index < 0 (an idle sequence) is not live: zero planes
+    const int64_t xg = t < tokens ? (rows ? static_cast<int64_t>(rows[t]) : t) : -1;
+    const bool live = xg >= 0;
+    const int64_t xr = live ? xg : 0;
     float* x = X + xr * k;
     if (Y) {
         float* y = Y + xr * k;  // partial tile 0 takes the sum

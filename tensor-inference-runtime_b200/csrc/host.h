@@ -128,7 +128,8 @@ int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* pla
                          bool pdl = false);
 // Planes of rmsnorm(X[r]) * w, r = rows ? rows[t] : t for t < tokens, after
 // X[r] += Y[r] when Y is not null, Y the sum of y_parts partial tiles y_part
-// floats apart (summed into tile 0).
+// floats apart (summed into tile 0).  Gathered rows must be distinct; a
+// negative rows[t] gives zero planes for t.
 int launch_gemm_norm_planes(float* X, float* Y, int y_parts, int64_t y_part, const int32_t* rows, int64_t tokens,
                             int64_t k, const float* w, float eps, uint8_t* planes, float* inv, void* stream,
                             bool pdl = false);

@@ -111,6 +111,8 @@ SIGNATURES = {
     "tir_test_forward": (C.c_int, [_vp, _i32p]),
     "tir_state_enable_dump": (C.c_int, [_vp, C.c_int32]),
     "tir_state_dump": (C.c_int, [_vp, _f32p]),
+    "tir_debug_dump_layers": (C.c_int, [_vp, _f32p]),
+    "tir_prefill": (C.c_int, [_vp, _vp, C.c_int32, C.c_int32, _vp]),
     "tir_state_enable_trace": (C.c_int, [_vp, C.c_int32]),
     "tir_state_trace_dims": (C.c_int, [_vp, _i32p, _i32p]),
     "tir_state_trace": (C.c_int, [_vp, C.POINTER(C.c_uint64)]),
@@ -138,6 +140,7 @@ SIGNATURES = {
     "tir_batch_stream": (_vp, [_vp]),
     "tir_batch_step": (C.c_int, [_vp, _vp, C.c_int32, _vp]),
     "tir_batch_generate": (C.c_int, [_vp, _vp, C.c_int32, C.c_int32, _vp]),
+    "tir_batch_logits": (C.c_int, [_vp, _vp]),
     "tir_q8_gemm_bytes": (_i64, [_i64, _i64]),
     "tir_q8_gemm_rows": (_i64, [_i64]),
     "tir_q8_gemm_prepare": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
@@ -492,6 +495,15 @@ class State:
                                       C.byref(n), C.byref(k)))
         return buf.raw[:min(n.value, cap - 1)].decode("utf-8"), k.value
 
+    def prefill(self, ids, want_logits=True):
+        """The prompt pass alone (positions 0..len-1 of an empty cache); the last
+        position's logits, or None."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        check(lib().tir_prefill(self._h, ids.ctypes.data, 1, len(ids),
+                                logits.ctypes.data if want_logits else None))
+        return logits
+
     def generate_capped_device(self, prompt_dev, n_prompt, cap, out_dev):
         check(lib().tir_generate_capped_device(self._h, _ptr(prompt_dev), n_prompt, cap,
                                                _ptr(out_dev)))
@@ -522,6 +534,12 @@ class State:
         check(lib().tir_state_dump(self._h, out.ctypes.data_as(_f32p)))
         return out
 
+    def dump_layers(self):
+        """[layers, embed_dim]: every layer's output in the last forward."""
+        out = np.empty((self.layers, self.embed_dim), np.float32)
+        check(lib().tir_debug_dump_layers(self._h, out.ctypes.data_as(_f32p)))
+        return out
+
 
 # ---------------------------------------------------------------------------
 # op level (device pointers)
@@ -550,6 +568,7 @@ class Batch:
     def __init__(self, model, n_seqs, max_ctx, max_tokens_per_seq, n_pages=None):
         self.model = model
         self.n_seqs = n_seqs
+        self.vocab = model.info["vocab"]
         h = C.c_void_p()
         if n_pages is None:
             check(lib().tir_batch_create(model.handle, n_seqs, max_ctx, max_tokens_per_seq, C.byref(h)))
@@ -613,6 +632,12 @@ class Batch:
         prompts = np.ascontiguousarray(prompts, np.int32).reshape(self.n_seqs, -1)
         out = np.zeros((self.n_seqs, cap), np.int32)
         check(lib().tir_batch_generate(self._h, prompts.ctypes.data, prompts.shape[1], cap, out.ctypes.data))
+        return out
+
+    def logits(self):
+        """[n_seqs, vocab]: each sequence's last-row logits of the last forward."""
+        out = np.empty((self.n_seqs, self.vocab), np.float32)
+        check(lib().tir_batch_logits(self._h, out.ctypes.data))
         return out
 
 

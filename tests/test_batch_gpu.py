@@ -141,3 +141,39 @@ def test_continuous_batching_reuses_pages(tirlib, orc, tiny):
     assert b.seq_len(0) == len(p0) + len(out0) - 1 and b.seq_len(1) == len(p2) + len(out2) - 1
     assert b.free_pages() == 1
     b.close()
+
+
+def test_batch_logits_match_each_sequence(tirlib, orc, small_path):
+    """tir_batch_logits: every sequence's last-row logits after a prefill step
+    and after a decode step agree with the oracle's forward of that sequence
+    alone, and their argmax is the step's greedy id."""
+    from oracle.gguf_ref import GGUF
+    from test_decode_gpu import rel_l2
+    m = tirlib.Model(small_path)
+    vocab = m.info["vocab"]
+    b = tirlib.Batch(m, 3, max_ctx=32, max_tokens_per_seq=8)
+    prompts = np.stack([synth.prompt_ids(8, vocab, seed=700 + i) for i in range(3)])
+    nxt = b.step(prompts)
+    lg = b.logits()
+    np.testing.assert_array_equal(np.argmax(lg[:, ::-1], axis=1) * -1 + vocab - 1, nxt)
+    om = orc.model(GGUF(small_path))
+    for i in range(3):
+        om.reset()
+        ref = None
+        for pos, t in enumerate(prompts[i]):
+            ref = om.forward(om.embed(int(t)), pos)
+        assert rel_l2(lg[i], ref) < 1e-4
+    nxt2 = b.step(nxt.reshape(3, 1))
+    lg2 = b.logits()
+    np.testing.assert_array_equal(np.argmax(lg2[:, ::-1], axis=1) * -1 + vocab - 1, nxt2)
+    # sequence 0 decodes while 1 and 2 idle: its logits are its own, theirs zero
+    nxt3 = b.step_ragged([[int(nxt2[0])], [], []])
+    lg3 = b.logits()
+    assert not lg3[1:].any()
+    om.reset()
+    for pos, t in enumerate(list(prompts[0]) + [int(nxt[0]), int(nxt2[0])]):
+        ref = om.forward(om.embed(int(t)), pos)
+    assert rel_l2(lg3[0], ref) < 1e-4
+    assert int(nxt3[0]) == vocab - 1 - int(np.argmax(lg3[0][::-1]))
+    b.close()
+    m.close()

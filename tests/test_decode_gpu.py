@@ -83,6 +83,28 @@ def test_per_layer_hidden_states(models, name):
     st.close()
 
 
+def test_prefill_and_layer_dump(models, tirlib):
+    """tir_prefill: the prompt pass alone (the logits generate_capped(prompt, 0)
+    leaves, and the oracle's after the same ids); tir_debug_dump_layers: the
+    layer outputs of the dump."""
+    m, om = models["small"]
+    ids = synth.prompt_ids(7, m.info["vocab"], seed=11)
+    st = m.state(max_ctx=16)
+    st.enable_dump(True)
+    lg = st.prefill(ids)
+    _, ref = st.generate_capped(ids, 0, want_logits=True)
+    np.testing.assert_array_equal(lg, ref)
+    np.testing.assert_array_equal(st.dump_layers(), st.dump()[1:])
+    om.reset()
+    for pos, t in enumerate(ids):
+        want = om.forward(om.embed(int(t)), pos)
+    assert rel_l2(lg, want) < LAYER_TOL
+    with pytest.raises(tirlib.TirError) as e:
+        tirlib.check(tirlib.lib().tir_prefill(st._h, ids.ctypes.data, 2, len(ids), None))
+    assert e.value.name == "INVALID_ARG"
+    st.close()
+
+
 def test_forward_by_token_equals_embedded(models):
     m, om = models["tiny"]
     a, b = m.state(max_ctx=16), m.state(max_ctx=16)
