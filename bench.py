@@ -73,6 +73,16 @@ def parse_args(argv=None):
 # ---------------------------------------------------------------------------
 # distributed plumbing (barrier + max over ranks); no collective on the data path
 # ---------------------------------------------------------------------------
+def decode_seed(seed, rank):
+    """Prompt seed of rank `rank`'s batch-1 sequence (each rank its own)."""
+    return seed + rank
+
+
+def batched_seed(seed, rank):
+    """Seed of rank `rank`'s batch of sequences (each rank its own shard)."""
+    return seed + 7919 * rank
+
+
 class Dist:
     def __init__(self, backend="nccl"):
         self.rank = int(os.environ.get("RANK", 0))
@@ -292,7 +302,7 @@ def run_ours(args, dist):
     st = model.state(max_ctx=n_fwd)
     stream = torch.cuda.ExternalStream(st.stream(), device=torch.device("cuda", dev))
     # each rank decodes its own sequence (weak scaling)
-    prompt = synth.prompt_ids(args.prompt, info["vocab"], seed=args.seed + dist.rank)
+    prompt = synth.prompt_ids(args.prompt, info["vocab"], seed=decode_seed(args.seed, dist.rank))
     d_prompt = torch.from_numpy(prompt.copy()).to(f"cuda:{dev}")
     d_out = torch.empty(args.decode, dtype=torch.int32, device=f"cuda:{dev}")
 
@@ -467,7 +477,7 @@ def run_batched(args, dist):
         B, P, cap = 64, 128, args.decode  # --decode shortens the run for profiling (default 128)
     else:
         B, P, cap = 16, 512, 0
-    rng = np.random.default_rng(args.seed + 7919 * dist.rank)
+    rng = np.random.default_rng(batched_seed(args.seed, dist.rank))
     prompts = rng.integers(3, V, size=(B, P), dtype=np.int32)
     batch = tir.Batch(model, B, max_ctx=P + cap + 1, max_tokens_per_seq=P)
     stream = torch.cuda.ExternalStream(batch.stream(), device=torch.device("cuda", dev))
