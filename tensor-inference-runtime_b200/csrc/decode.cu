@@ -482,10 +482,10 @@ __device__ __forceinline__ void pack_digits(const uint32_t* u, uint32_t& w0, uin
 // fma(value, 2^(22-E), 1.5 * 2^23) has q in its low mantissa bits, and adding
 // 0x408080 leaves u = q + 0x808080 in bytes 0..2, i.e. digit + 128 per byte
 // (q = d0 + 256 d1 + 65536 d2, |d2| <= 64).  Blocks with m < 2^-86 use E = -86.
-// For the step input, the CTA owning a chunk also materialises it as the
+// For the step input, one of the phase's CTAs also stores each chunk as the
 // residual stream x (and dump row 0).
 __device__ __forceinline__ void stage_load(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
-                                           const Prefetch& pf, float* v, float& inv, float& rms) {
+                                           const Prefetch& pf, float* v, float& inv, float& rms, int ph) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = d.k, nchunks = K / 16;
     const bool norm = d.in_kind == IN_X_NORM || d.in_kind == IN_X0_NORM;
@@ -517,7 +517,9 @@ __device__ __forceinline__ void stage_load(const DecodeParams& p, Smem& s, const
     } else if (c < nchunks) {
         load16(p, d, st, c * 16, v);
     }
-    if (d.in_kind == IN_X0_NORM && c < nchunks && c % static_cast<int>(gridDim.x) == static_cast<int>(blockIdx.x)) {
+    // chunk c is stored by one of the phase's CTAs with tiles (only they
+    // stage), told apart by their first tile
+    if (d.in_kind == IN_X0_NORM && c < nchunks && c % min(d.n_tiles, static_cast<int>(gridDim.x)) == s.tfirst[ph]) {
         float4* x4 = reinterpret_cast<float4*>(p.x + c * 16);
         float4* d4 = p.dump ? reinterpret_cast<float4*>(p.dump + c * 16) : nullptr;
 #pragma unroll
@@ -547,10 +549,10 @@ __device__ __forceinline__ void stage_load(const DecodeParams& p, Smem& s, const
 }
 
 __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, const PhaseDesc& d, const StepCtx& st,
-                                            const Prefetch& pf) {
+                                            const Prefetch& pf, int ph) {
     const int c = threadIdx.x, nchunks = d.k / 16;
     float v[16], inv, rms;
-    stage_load(p, s, d, st, pf, v, inv, rms);
+    stage_load(p, s, d, st, pf, v, inv, rms, ph);
     float mx = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) mx = fmaxf(mx, fabsf(v[i]));
@@ -586,10 +588,10 @@ __device__ __forceinline__ void stage_input(const DecodeParams& p, Smem& s, cons
 // the exact integer block dot times scale_a * scale_w.  Compiled only into
 // the kernel instantiation for Mode::Quantize (decode_kernel<true>).
 __device__ __forceinline__ void stage_input_qact(const DecodeParams& p, Smem& s, const PhaseDesc& d,
-                                                 const StepCtx& st, const Prefetch& pf) {
+                                                 const StepCtx& st, const Prefetch& pf, int ph) {
     const int c = threadIdx.x, nchunks = d.k / 16;
     float v[16], inv, rms;
-    stage_load(p, s, d, st, pf, v, inv, rms);
+    stage_load(p, s, d, st, pf, v, inv, rms, ph);
     uint32_t babs = 0u;
     float bval = 0.f;
 #pragma unroll
@@ -828,9 +830,9 @@ __device__ __forceinline__ bool gemv_phase(const DecodeParams& p, Smem& s, Strea
         return true;
     }
     if (QACT && d.qact)
-        stage_input_qact(p, s, d, st, pf);
+        stage_input_qact(p, s, d, st, pf, ph);
     else
-        stage_input(p, s, d, st, pf);
+        stage_input(p, s, d, st, pf, ph);
     trace_mark(p, ph, st.f, 2);
     unsigned long long best = 0ull;
     bool ok;
