@@ -495,14 +495,14 @@ def run_batched(args, dist):
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     dist.barrier()
     torch.cuda.synchronize(dev)
-    t0 = time.perf_counter()
     with ClockSampler(uuid) as clocks:
+        t0 = time.perf_counter()  # after the sampler's start-up, which is not the workload's
         ev[0].record(stream)
         for i in range(args.steps):
             step()
             ev[i + 1].record(stream)
         torch.cuda.synchronize(dev)
-    wall_ms = (time.perf_counter() - t0) / args.steps * 1e3
+        wall_ms = (time.perf_counter() - t0) / args.steps * 1e3
     ms_local = sum(ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)) / args.steps
     dist.barrier()
     ms = dist.max(ms_local)
