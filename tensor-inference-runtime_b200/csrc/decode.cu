@@ -1034,37 +1034,57 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
                 prefetch_operands(p, d, st, pf);
             else if (tid == 0)
                 prefetched = attn_prefetch(p, s, d, st);
-            // 1. dependency on the previous phase (bounded), by thread 0
-            if (tid == 0) {
-                const uint64_t w0 = tr.on ? globaltimer_ns() : 0;
-                bool ok = true;
-                if (ph > 0)
-                    ok = wait_counter(p, p.counters + ph - 1, static_cast<uint32_t>((f + 1) * G), ph, f);
-                else if (f > 0)
-                    ok = wait_counter(p, p.counters + p.n_phases - 1, static_cast<uint32_t>(f * G), ph, f);
-                if (tr.on) tr.dep_wait_ns += globaltimer_ns() - w0;
+            // 1. dependency on the previous phase (bounded), by thread 0; warp 0
+            //    then reads the step's token
+            if (tid < 32) {
+                int ok = 1;
+                if (tid == 0) {
+                    const uint64_t w0 = tr.on ? globaltimer_ns() : 0;
+                    if (ph > 0)
+                        ok = wait_counter(p, p.counters + ph - 1, static_cast<uint32_t>((f + 1) * G), ph, f) ? 1 : 0;
+                    else if (f > 0)
+                        ok = wait_counter(p, p.counters + p.n_phases - 1, static_cast<uint32_t>(f * G), ph, f) ? 1 : 0;
+                    if (tr.on) tr.dep_wait_ns += globaltimer_ns() - w0;
+                }
+                ok = __shfl_sync(FULL, ok, 0);
+                __syncwarp();  // the other lanes read what thread 0's acquire covers
                 if (ok && d.kind == PH_GEMV && d.in_kind == IN_X0_NORM) {
                     // The step's token: prompt id, or greedy argmax of the
-                    // previous step's logits (src/tokenizer.rs:152-167).
+                    // previous step's logits (src/tokenizer.rs:152-167): the
+                    // CTAs' candidates (value key << 32 | index, so the max
+                    // keeps the last of equal values) loaded by all 32 lanes
+                    // at once and reduced over the warp.
                     int tok = 0;
                     if (f < p.n_prompt) {
                         tok = p.prompt ? p.prompt[f] : 0;
                     } else if (f > 0) {
+                        unsigned long long c8[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int c = tid + 32 * i;
+                            c8[i] = c < G ? __ldcg(p.argmax_part + c) : 0ull;
+                        }
                         unsigned long long b = 0ull;
-                        for (int c = 0; c < G; ++c) b = max(b, __ldcg(p.argmax_part + c));
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) b = max(b, c8[i]);
+                        for (int c = tid + 256; c < G; c += 32) b = max(b, __ldcg(p.argmax_part + c));
+#pragma unroll
+                        for (int o = 16; o; o >>= 1) b = max(b, __shfl_xor_sync(FULL, b, o));
                         tok = static_cast<int>(b & 0xffffffffu);
                     }
-                    // Ids from device memory are unchecked by the host: an id
-                    // outside the vocabulary is reported, and row 0 is read
-                    // instead so no access leaves the embedding table.
-                    if (tok < 0 || tok >= p.vocab) {
-                        set_error(p, kErrBadToken, ph, f);
-                        tok = 0;
+                    if (tid == 0) {
+                        // Ids from device memory are unchecked by the host: an id
+                        // outside the vocabulary is reported, and row 0 is read
+                        // instead so no access leaves the embedding table.
+                        if (tok < 0 || tok >= p.vocab) {
+                            set_error(p, kErrBadToken, ph, f);
+                            tok = 0;
+                        }
+                        s.token = tok;
+                        if (blockIdx.x == 0 && f >= p.n_prompt && p.out_ids) p.out_ids[f - p.n_prompt] = tok;
                     }
-                    s.token = tok;
-                    if (blockIdx.x == 0 && f >= p.n_prompt && p.out_ids) p.out_ids[f - p.n_prompt] = tok;
                 }
-                s.phase_ok = ok ? 1 : 0;
+                if (tid == 0) s.phase_ok = ok;
             }
             cbar();
             if (!s.phase_ok) {
