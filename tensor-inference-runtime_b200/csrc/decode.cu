@@ -978,15 +978,32 @@ __device__ __forceinline__ bool attention_phase(const DecodeParams& p, Smem& s, 
             for (int h = warp; h < group; h += kWarps) {
                 const float* base = p.attn_part + (static_cast<size_t>(g) * p.max_splits * group + h) * kAttnRec;
                 const size_t jstride = static_cast<size_t>(group) * kAttnRec;
+                // the splits' maxima, lanes over splits; then the records in
+                // batches of 4 whose loads are all in flight at once, folded
+                // in split order (the same sums as one split at a time)
                 float M = -INFINITY;
-                for (int jj = 0; jj < S; ++jj) M = fmaxf(M, __ldcg(base + jj * jstride));
+                for (int jj = lane; jj < S; jj += 32) M = fmaxf(M, __ldcg(base + jj * jstride));
+                M = warp_max(M);
                 float L = 0.f, O0 = 0.f, O1 = 0.f;
-                for (int jj = 0; jj < S; ++jj) {
-                    const float* pj = base + jj * jstride;
-                    const float w = expf(__ldcg(pj) - M);
-                    L = fmaf(__ldcg(pj + 1), w, L);
-                    O0 = fmaf(__ldcg(pj + 4 + lane), w, O0);
-                    O1 = fmaf(__ldcg(pj + 4 + lane + 32), w, O1);
+                for (int j0 = 0; j0 < S; j0 += 4) {
+                    float m4[4], l4[4], a4[4], b4[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float* pj = base + static_cast<size_t>(min(j0 + i, S - 1)) * jstride;
+                        m4[i] = __ldcg(pj);
+                        l4[i] = __ldcg(pj + 1);
+                        a4[i] = __ldcg(pj + 4 + lane);
+                        b4[i] = __ldcg(pj + 4 + lane + 32);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (j0 + i < S) {
+                            const float w = expf(m4[i] - M);
+                            L = fmaf(l4[i], w, L);
+                            O0 = fmaf(a4[i], w, O0);
+                            O1 = fmaf(b4[i], w, O1);
+                        }
+                    }
                 }
                 float* out = p.attn_out + static_cast<size_t>(g * group + h) * kHeadDim;
                 out[lane] = O0 / L;
