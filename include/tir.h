@@ -290,6 +290,15 @@ tir_status tir_batch_generate(tir_batch *b, const int32_t *prompts_host, int32_t
  * [n_seqs][vocab] (forward's return value, src/forward.rs:242-252, per
  * sequence; a sequence idle in that step gets zeros). */
 tir_status tir_batch_logits(tir_batch *b, float *logits_host);
+/* Per-layer outputs of chosen step rows, for layer-by-layer comparison with
+ * the reference's forward (src/forward.rs:13-258; the batched counterpart of
+ * tir_debug_dump_layers).  tir_batch_dump_rows arms a dump of rows_host[i]
+ * (indices into the step's rows, sequence-major) for every later forward run
+ * outside the captured decode graph (prefill and ragged steps; n_rows = 0
+ * disarms); tir_batch_dump copies [n_rows][layers][embed_dim] of the last
+ * such forward to out_host. */
+tir_status tir_batch_dump_rows(tir_batch *b, const int32_t *rows_host, int32_t n_rows);
+tir_status tir_batch_dump(tir_batch *b, float *out_host);
 
 /* ---- op-level kernels (device pointers, asynchronous on `stream`) --------- */
 
@@ -353,15 +362,15 @@ void tir_rope_angles(float base, int64_t pos, int64_t dim, float *out_host);
 tir_status tir_swiglu(const float *x, const uint8_t *gate_q, const uint16_t *gate_s,
                       const uint8_t *up_q, const uint16_t *up_s, const uint8_t *down_q,
                       const uint16_t *down_s, float *out, int64_t k, int64_t f, void *stream);
-/* tir_swiglu without device allocation.  No counterpart in the reference (its
- * swiglu, src/math.rs:164-178, allocates host Vecs per call); this is for
- * callers that must not allocate device memory while they run.  Same inputs
+/* tir_swiglu without device allocation.  No counterpart in the reference; this
+ * is for callers that must not allocate device memory while they run.  Same inputs
  * and results as tir_swiglu, but gate, up and silu(gate)*up live in a fixed
  * per-device static array, so f <= 6144 (k <= 6144 as for tir_swiglu); larger
  * sizes return TIR_ERR_UNSUPPORTED_SHAPE.  Makes no cudaMalloc/cudaFree call.
  * The first call on a device looks the array's address up (cudaGetSymbolAddress)
  * with that device current; make it before any stream capture on the device.
- * Calls on the same device must not overlap in time: they share the array. */
+ * Calls on the same device must not overlap in time: they share the array.
+ * A device-side wait that runs out is reported by tir_ops_check. */
 tir_status tir_swiglu_static(const float *x, const uint8_t *gate_q, const uint16_t *gate_s,
                              const uint8_t *up_q, const uint16_t *up_s, const uint8_t *down_q,
                              const uint16_t *down_s, float *out, int64_t k, int64_t f,
@@ -382,6 +391,37 @@ tir_status tir_argmax(const float *x, int64_t n, int32_t *out_id, void *stream);
 tir_status tir_attention(const float *q, const float *k_cache, const float *v_cache,
                          float *out, int64_t q_heads, int64_t k_v_heads, int64_t dim,
                          int64_t n_ctx, int64_t max_ctx, void *stream);
+
+/* The op entry points above run asynchronously on the caller's stream, so a
+ * bounded device-side wait that gave up (TIR_TIMEOUT_MS) inside one of them
+ * cannot be returned by the call itself.  tir_ops_check synchronises `stream`
+ * and returns TIR_ERR_TIMEOUT if any op launched on the current device since
+ * the last check recorded one (tir_q8_matmul*, tir_swiglu*,
+ * tir_q8_matmul_batch), clearing the record; TIR_OK otherwise.  Each op
+ * clears its launch's own error words first, so one failure does not make
+ * later calls skip their work.  Runtime extension; no counterpart in the
+ * reference, whose ops are synchronous CPU code. */
+tir_status tir_ops_check(void *stream);
+
+/* ---- test hooks (runtime extensions; no counterpart in the reference) ----
+ * tir_debug_fail_alloc_after(n): the n-th next allocation the library makes
+ * (device, stream-ordered or pinned host; n = 0 is the next one) fails once
+ * with TIR_ERR_OOM, driving the failure branches of model load and
+ * state/batch creation (the reference's ModelLoadError, src/error.rs:49-59,
+ * covers the same load step).  n < 0 disarms.
+ * tir_debug_alloc_count: allocations attempted so far (all kinds).
+ * tir_debug_hold_phase(s, phase, timeout_us): the next decode launch of `s`
+ * waits for one release more than the grid makes at `phase` (>= 1) with a
+ * limit of timeout_us, so that wait runs out on purpose: the launch returns
+ * TIR_ERR_TIMEOUT and resets the state, whose next call decodes normally.
+ * tir_debug_hold_next_op(timeout_us): the next streaming Q8_0 matvec
+ * (tir_q8_matmul, _qact, _tiled, or one inside tir_swiglu) completes its
+ * output, then runs a second pass whose start waits for a release that never
+ * comes and gives up after timeout_us; tir_ops_check then reports it. */
+void tir_debug_fail_alloc_after(int64_t n);
+tir_status tir_debug_hold_next_op(int32_t timeout_us);
+int64_t tir_debug_alloc_count(void);
+tir_status tir_debug_hold_phase(tir_state *s, int32_t phase, int32_t timeout_us);
 
 #ifdef __cplusplus
 }

@@ -66,6 +66,7 @@ class Oracle:
             "orc_generate_capped": (C.c_int, [C.POINTER(Dims), C.POINTER(C.c_void_p), _i32p,
                                               C.c_size_t, C.c_size_t, _i32p, _f32p]),
             "orc_set_threads": (None, [C.c_int]),
+            "orc_set_fast": (None, [C.c_int]),
             "orc_get_threads": (C.c_int, []),
         }
         for name, (res, args) in sig.items():
@@ -168,6 +169,10 @@ class Oracle:
 
     def set_threads(self, n):
         self.lib.orc_set_threads(int(n))
+
+    def set_fast(self, on):
+        """Eight rows per pass and parallel attention heads: the same bits, faster."""
+        self.lib.orc_set_fast(1 if on else 0)
 
     def get_threads(self):
         return self.lib.orc_get_threads()

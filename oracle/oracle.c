@@ -19,8 +19,16 @@
 #define RUST_SUM_INIT (-0.0f)
 
 static int g_threads = 0;
+/* 0: one matrix row at a time and attention heads in order, as the reference
+ * loops (the CPU baseline times this); 1: eight rows per pass and attention
+ * heads in parallel, for the tests.  Every row and every head performs the
+ * same operations in the same order either way, so the results are
+ * bit-identical (tests/test_oracle_kat.py checks it). */
+static int g_fast = 0;
 
 void orc_set_threads(int n) { g_threads = n; }
+
+void orc_set_fast(int on) { g_fast = on ? 1 : 0; }
 
 int orc_get_threads(void) {
 #ifdef _OPENMP
@@ -147,12 +155,41 @@ float orc_dot_prod_act_q8(const uint8_t *a, const uint8_t *b, size_t k) {
     return total;
 }
 
+/* orc_dot_prod_q8 of eight consecutive rows at once: each row's sums take the
+ * same operations in the same order as orc_dot_prod_q8's (the eight chains
+ * are independent, so they only overlap in time). */
+static void dot_prod_q8_x8(const float *a, const uint8_t *b, size_t row_bytes, size_t k, float *out) {
+    float sum[8], block_sum[8], scale[8];
+    for (int r = 0; r < 8; r++) sum[r] = 0.0f;
+    for (size_t blk = 0; blk < k / 32; blk++) {
+        const float *ab = a + blk * 32;
+        for (int r = 0; r < 8; r++) {
+            scale[r] = block_scale(b + r * row_bytes + blk * 34);
+            block_sum[r] = RUST_SUM_INIT;
+        }
+        float qf[32][8]; /* the block's weights, row-interleaved */
+        for (int r = 0; r < 8; r++)
+            for (int i = 0; i < 32; i++) qf[i][r] = (float)(int8_t)b[r * row_bytes + blk * 34 + 2 + i];
+        for (int i = 0; i < 32; i++)
+            for (int r = 0; r < 8; r++) block_sum[r] += ab[i] * qf[i][r];
+        for (int r = 0; r < 8; r++) sum[r] += block_sum[r] * scale[r];
+    }
+    for (int r = 0; r < 8; r++) out[r] = sum[r];
+}
+
 /* src/math.rs:87-98: 64-row chunks in parallel; each row is one sequential
  * dot, so the result does not depend on the thread count. */
 void orc_q8_matmul(const float *a, const uint8_t *b, float *out, size_t n, size_t k) {
     size_t row_bytes = k / 32 * 34;
     int nt = orc_get_threads();
     (void)nt;
+    if (g_fast) {
+        long n8 = (long)(n / 8);
+#pragma omp parallel for schedule(static, 8) num_threads(nt)
+        for (long g = 0; g < n8; g++) dot_prod_q8_x8(a, b + (size_t)g * 8 * row_bytes, row_bytes, k, out + g * 8);
+        for (size_t r = (size_t)n8 * 8; r < n; r++) out[r] = orc_dot_prod_q8(a, b + r * row_bytes, k);
+        return;
+    }
 #pragma omp parallel for schedule(static, 64) num_threads(nt)
     for (long r = 0; r < (long)n; r++) out[r] = orc_dot_prod_q8(a, b + (size_t)r * row_bytes, k);
 }
@@ -358,25 +395,34 @@ int orc_forward(const orc_dims *d, const void *const *T, orc_cache *cache,
         /* :83-84 append to the cache */
         cache_extend(cache, key, value, KVD);
 
-        /* :86-174 grouped-query attention over positions pos, pos-1, ..., 0 */
+        /* :86-174 grouped-query attention over positions pos, pos-1, ..., 0;
+         * query head h uses kv head h / group.  Heads are independent: in
+         * fast mode they run in parallel, each on its own score buffers. */
         float sq = sqrtf((float)hd);
-        for (size_t g = 0; g < nkv; g++) {
-            for (size_t hi = 0; hi < group; hi++) {
-                size_t h = g * group + hi;
-                const float *qv = query + h * hd;
-                for (size_t j = 0; j <= pos; j++) {
-                    size_t t = pos - j;
-                    const float *kv = cache->key_cache + t * L * KVD + l * KVD + g * hd;
-                    scores[j] = orc_dot_prod_f32(qv, kv, hd) / sq;
-                }
-                orc_softmax(scores, probs, pos + 1);
-                float *w = weighted_values + h * hd;
-                for (size_t e = 0; e < hd; e++) w[e] = 0.0f;
-                for (size_t j = 0; j <= pos; j++) {
-                    size_t t = pos - j;
-                    const float *vv = cache->value_cache + t * L * KVD + l * KVD + g * hd;
-                    for (size_t e = 0; e < hd; e++) w[e] = w[e] + vv[e] * probs[j];
-                }
+        int nt_attn = g_fast ? orc_get_threads() : 1;
+        (void)nt_attn;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt_attn)
+        for (long hl = 0; hl < (long)nq; hl++) {
+            size_t h = (size_t)hl, g = h / group;
+            float *sc = g_fast ? (float *)malloc((pos + 1) * sizeof(float)) : scores;
+            float *pr = g_fast ? (float *)malloc((pos + 1) * sizeof(float)) : probs;
+            const float *qv = query + h * hd;
+            for (size_t j = 0; j <= pos; j++) {
+                size_t t = pos - j;
+                const float *kv = cache->key_cache + t * L * KVD + l * KVD + g * hd;
+                sc[j] = orc_dot_prod_f32(qv, kv, hd) / sq;
+            }
+            orc_softmax(sc, pr, pos + 1);
+            float *w = weighted_values + h * hd;
+            for (size_t e = 0; e < hd; e++) w[e] = 0.0f;
+            for (size_t j = 0; j <= pos; j++) {
+                size_t t = pos - j;
+                const float *vv = cache->value_cache + t * L * KVD + l * KVD + g * hd;
+                for (size_t e = 0; e < hd; e++) w[e] = w[e] + vv[e] * pr[j];
+            }
+            if (g_fast) {
+                free(sc);
+                free(pr);
             }
         }
 

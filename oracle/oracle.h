@@ -105,6 +105,9 @@ int orc_generate_capped(const orc_dims *d, const void *const *tensors,
 
 /* Thread count used by the parallel matvecs (Rayon's pool in the reference). */
 void orc_set_threads(int n);
+/* 1: eight matrix rows per pass and attention heads in parallel (same bits,
+ * faster; for the tests); 0 (default): the reference's loop order. */
+void orc_set_fast(int on);
 int orc_get_threads(void);
 
 #ifdef __cplusplus

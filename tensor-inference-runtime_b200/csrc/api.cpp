@@ -10,6 +10,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -43,6 +44,47 @@ static tir_status cuda_fail(cudaError_t e, const char* what) {
         cudaError_t e_ = (expr);                     \
         if (e_ != cudaSuccess) return cuda_fail(e_, what); \
     } while (0)
+
+// Every allocation the library makes (device, stream-ordered and pinned host)
+// goes through these: they count the calls (tir_debug_alloc_count) and, when
+// armed by tir_debug_fail_alloc_after(n), make the n-th next call fail once
+// with cudaErrorMemoryAllocation, so the load / create paths' OOM branches can
+// be driven without exhausting a GPU.
+static std::atomic<long long> g_alloc_calls{0};
+static std::atomic<long long> g_alloc_fail_in{-1};
+
+static bool alloc_injected_failure() {
+    g_alloc_calls.fetch_add(1);
+    long long n = g_alloc_fail_in.load();
+    while (n >= 0) {
+        if (g_alloc_fail_in.compare_exchange_weak(n, n - 1)) return n == 0;
+    }
+    return false;
+}
+
+cudaError_t dev_malloc(void** p, size_t bytes) {
+    if (alloc_injected_failure()) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMalloc(p, bytes);
+}
+
+cudaError_t dev_malloc_async(void** p, size_t bytes, cudaStream_t stream) {
+    if (alloc_injected_failure()) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMallocAsync(p, bytes, stream);
+}
+
+cudaError_t host_malloc_pinned(void** p, size_t bytes) {
+    if (alloc_injected_failure()) {
+        *p = nullptr;
+        return cudaErrorMemoryAllocation;
+    }
+    return cudaMallocHost(p, bytes);
+}
 
 // Rows per weight tile of a matrix with k columns (gemv_tile_rows, even, so
 // fused pairs -- RoPE, gate|up -- never straddle tiles); 0 if k is not a
@@ -84,8 +126,12 @@ static DevCtx* dev_ctx(int device) {
     if (device >= static_cast<int>(ctxs.size())) ctxs.resize(device + 1, nullptr);
     if (!ctxs[device]) {
         DevCtx* c = new DevCtx;
-        if (cudaMalloc(&c->counters, 64) != cudaSuccess || cudaMalloc(&c->error, 64) != cudaSuccess ||
-            cudaMalloc(&c->argmax, 8 * 1024) != cudaSuccess) {
+        if (dev_malloc(reinterpret_cast<void**>(&c->counters), 64) != cudaSuccess ||
+            dev_malloc(reinterpret_cast<void**>(&c->error), 64) != cudaSuccess ||
+            dev_malloc(reinterpret_cast<void**>(&c->argmax), 8 * 1024) != cudaSuccess) {
+            cudaFree(c->counters);  // cudaFree(nullptr) is a no-op
+            cudaFree(c->error);
+            cudaFree(c->argmax);
             delete c;
             return nullptr;
         }
@@ -96,12 +142,23 @@ static DevCtx* dev_ctx(int device) {
     return ctxs[device];
 }
 
-static unsigned long long timeout_ns() {
+unsigned long long timeout_ns() {
     const char* e = std::getenv("TIR_TIMEOUT_MS");
     long long ms = e ? std::atoll(e) : 2000;
     if (ms <= 0) ms = 2000;
     return static_cast<unsigned long long>(ms) * 1000000ull;
 }
+
+// Words 0..2 of an op's error block make a launch's waits give up at once;
+// they are cleared on the launch's stream before every launch.  Word 3 keeps
+// the code of a failure until tir_ops_check collects it.
+static cudaError_t clear_launch_error(uint32_t* err, void* stream) {
+    return cudaMemsetAsync(err, 0, 3 * sizeof(uint32_t), static_cast<cudaStream_t>(stream));
+}
+
+// tir_debug_hold_next_op: microseconds of the held second pass of the next
+// streaming matvec (0: none).
+static std::atomic<int> g_hold_next_op_us{0};
 
 tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_t* scales, float* out, int64_t n,
                             int64_t k, void* stream, bool qact) {
@@ -135,7 +192,16 @@ tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_
     p.error = c->error;
     p.argmax_part = c->argmax;
     p.timeout_ns = timeout_ns();
+    p.hold_phase = -1;
+    if (const int us = g_hold_next_op_us.exchange(0); us > 0) {
+        // a second pass of the same matvec whose start waits for one release
+        // more than the grid makes: it gives up after `us` and records it
+        p.n_steps = 2;
+        p.hold_phase = 0;
+        p.timeout_ns = static_cast<unsigned long long>(us) * 1000ull;
+    }
     const int grid = d.n_tiles < sms ? d.n_tiles : sms;
+    CUDA_TRY(clear_launch_error(c->error, stream), "error reset");
     const int rc = decode_launch(p, grid, stream, false);
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "q8 matvec launch");
     return TIR_OK;
@@ -175,6 +241,8 @@ struct tir_state {
     bool dump_on = false;
     unsigned long long* trace = nullptr;
     int32_t trace_step = -1;
+    int32_t hold_phase = -1;                // tir_debug_hold_phase, next launch only
+    unsigned long long hold_timeout_ns = 0;
     int32_t* h_ids = nullptr;  // pinned, max_ctx
     uint32_t* h_err = nullptr; // pinned, 4
     ~tir_state() {
@@ -459,7 +527,7 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
     plan(m->embd, static_cast<int64_t>(V), static_cast<int64_t>(H));
     const size_t on_off = plan_f32(static_cast<int64_t>(H));
     m->dev_bytes = off;
-    cudaError_t e = cudaMalloc(&m->dev, off);
+    cudaError_t e = dev_malloc(&m->dev, off);
     if (e != cudaSuccess) {
         delete m;
         return cuda_fail(e, "weight allocation");
@@ -486,7 +554,7 @@ tir_status tir_model_load_gguf(const tir_gguf* g, int device, tir_model** out) {
         for (const TensorInfo* ti : {x.q, x.k, x.v, x.o, x.gt, x.up, x.dn})
             if (ti->data_bytes > staging_bytes) staging_bytes = ti->data_bytes;
     uint8_t* staging = nullptr;
-    e = cudaMalloc(&staging, staging_bytes);
+    e = dev_malloc(&staging, staging_bytes);
     if (e != cudaSuccess) {
         delete m;
         return cuda_fail(e, "staging allocation");
@@ -630,12 +698,12 @@ static tir_status build_phases(tir_state* s) {
     s->n_phases = static_cast<int>(ph.size());
     s->mode = t.mode;
     void* p = nullptr;
-    CUDA_TRY(cudaMalloc(&p, ph.size() * sizeof(PhaseDesc)), "phase table");
+    CUDA_TRY(dev_malloc(&p, ph.size() * sizeof(PhaseDesc)), "phase table");
     s->allocs.push_back(p);
     s->d_phases = static_cast<PhaseDesc*>(p);
     CUDA_TRY(cudaMemcpy(p, ph.data(), ph.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice), "phase table upload");
     void* c = nullptr;
-    CUDA_TRY(cudaMalloc(&c, ph.size() * sizeof(uint32_t)), "phase counters");
+    CUDA_TRY(dev_malloc(&c, ph.size() * sizeof(uint32_t)), "phase counters");
     s->allocs.push_back(c);
     s->counters = static_cast<uint32_t*>(c);
     return TIR_OK;
@@ -665,7 +733,7 @@ tir_status tir_state_create(tir_model* m, int32_t max_ctx, tir_state** out) {
     if (ms < 1) ms = 1;
     s->max_splits = static_cast<int>(ms);
     auto alloc = [&](size_t bytes, void** p) -> bool {
-        if (cudaMalloc(p, bytes ? bytes : 16) != cudaSuccess) return false;
+        if (dev_malloc(p, bytes ? bytes : 16) != cudaSuccess) return false;
         s->allocs.push_back(*p);
         return true;
     };
@@ -689,8 +757,8 @@ tir_status tir_state_create(tir_model* m, int32_t max_ctx, tir_state** out) {
         delete s;
         return fail(TIR_ERR_OOM, "state allocation failed (KV cache of " + std::to_string(max_ctx) + " positions)");
     }
-    if (cudaMallocHost(&s->h_ids, static_cast<size_t>(max_ctx) * 4) != cudaSuccess ||
-        cudaMallocHost(&s->h_err, 16) != cudaSuccess) {
+    if (host_malloc_pinned(&s->h_ids, static_cast<size_t>(max_ctx) * 4) != cudaSuccess ||
+        host_malloc_pinned(&s->h_err, 16) != cudaSuccess) {
         delete s;
         return fail(TIR_ERR_OOM, "pinned host allocation failed");
     }
@@ -769,7 +837,9 @@ static tir_status launch_steps(tir_state* s, int n_steps, int pos0, const float*
     p.counters = s->counters;
     p.argmax_part = s->argmax_part;
     p.error = s->error;
-    p.timeout_ns = timeout_ns();
+    p.timeout_ns = s->hold_phase >= 0 ? s->hold_timeout_ns : timeout_ns();
+    p.hold_phase = s->hold_phase;
+    s->hold_phase = -1;
     p.trace = s->trace_step >= 0 ? s->trace : nullptr;
     p.trace_step = s->trace_step;
     CUDA_TRY(cudaMemsetAsync(s->counters, 0, static_cast<size_t>(s->n_phases) * 4, s->stream), "counter reset");
@@ -1011,7 +1081,7 @@ tir_status tir_state_enable_trace(tir_state* s, int32_t step) {
     if (step >= 0 && !s->trace) {
         void* p = nullptr;
         const size_t bytes = static_cast<size_t>(s->n_phases) * s->grid * kTraceFields * 8;
-        CUDA_TRY(cudaMalloc(&p, bytes), "trace buffer");
+        CUDA_TRY(dev_malloc(&p, bytes), "trace buffer");
         s->allocs.push_back(p);
         s->trace = static_cast<unsigned long long*>(p);
         CUDA_TRY(cudaMemset(p, 0, bytes), "trace buffer");
@@ -1138,11 +1208,12 @@ tir_status tir_q8_matmul_batch(const float* x, int64_t tokens, const uint8_t* w,
     const size_t pbytes = static_cast<size_t>(gemm_x_plane_bytes(tokens, k));
     const size_t ibytes = static_cast<size_t>(gemm_tokens_padded(tokens)) * 4;
     const size_t sbytes = splits > 1 ? static_cast<size_t>(splits) * tokens * n * 4 : 0;
-    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&planes), pbytes + ibytes + sbytes, st),
+    CUDA_TRY(dev_malloc_async(reinterpret_cast<void**>(&planes), pbytes + ibytes + sbytes, st),
              "batched matmul scratch");
     float* inv = reinterpret_cast<float*>(planes + pbytes);
     float* part = splits > 1 ? reinterpret_cast<float*>(planes + pbytes + ibytes) : y;
-    int rc = launch_gemm_x_planes(x, tokens, k, planes, inv, stream);
+    int rc = static_cast<int>(clear_launch_error(c->error, stream));
+    if (rc == 0) rc = launch_gemm_x_planes(x, tokens, k, planes, inv, stream);
     if (rc == 0) rc = launch_gemm_q8(w, w_pow2, planes, inv, n, k, tokens, part, n, splits, c->error, timeout_ns(), stream);
     if (rc == 0 && splits > 1) rc = launch_gemm_sum_parts(part, splits, tokens * n, tokens * n, y, stream);
     cudaFreeAsync(planes, st);
@@ -1203,7 +1274,7 @@ tir_status tir_swiglu(const float* x, const uint8_t* gate_q, const uint16_t* gat
         return fail(TIR_ERR_UNSUPPORTED_SHAPE, "swiglu needs k, f multiples of 32 and <= " + std::to_string(kMaxK));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* tmp = nullptr;
-    CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&tmp), static_cast<size_t>(3 * f) * 4, st), "swiglu scratch");
+    CUDA_TRY(dev_malloc_async(reinterpret_cast<void**>(&tmp), static_cast<size_t>(3 * f) * 4, st), "swiglu scratch");
     tir_status rc = q8_matmul_stream(x, gate_q, gate_s, tmp, f, k, stream);
     if (rc == TIR_OK) rc = q8_matmul_stream(x, up_q, up_s, tmp + f, f, k, stream);
     if (rc == TIR_OK) rc = op_rc(launch_silu_mul(tmp, tmp + f, tmp + 2 * f, f, stream), "silu");
@@ -1230,6 +1301,45 @@ tir_status tir_argmax(const float* x, int64_t n, int32_t* out_id, void* stream) 
     clear_error();
     if (n < 0) return fail(TIR_ERR_INVALID_ARG, "negative size");
     return op_rc(launch_argmax(x, n, out_id, stream), "argmax");
+}
+
+tir_status tir_ops_check(void* stream) {
+    clear_error();
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "stream synchronize");
+    uint32_t code = 0;
+    DevCtx* c = dev_ctx(dev);
+    if (!c) return fail(TIR_ERR_OOM, "device context allocation failed");
+    CUDA_TRY(cudaMemcpy(&code, c->error + 3, sizeof(uint32_t), cudaMemcpyDeviceToHost), "op error readback");
+    if (code != 0u) CUDA_TRY(cudaMemset(c->error + 3, 0, sizeof(uint32_t)), "op error reset");
+    uint32_t scode = 0;
+    const tir_status rc = static_scratch_take_error(dev, &scode);
+    if (rc != TIR_OK) return rc;
+    if (code != 0u || scode != 0u)
+        return fail(TIR_ERR_TIMEOUT, "a device-side wait of an op launched on device " + std::to_string(dev) +
+                                         " gave up (TIR_TIMEOUT_MS); its outputs are incomplete");
+    return TIR_OK;
+}
+
+void tir_debug_fail_alloc_after(int64_t n) { g_alloc_fail_in.store(n < 0 ? -1 : static_cast<long long>(n)); }
+
+int64_t tir_debug_alloc_count(void) { return static_cast<int64_t>(g_alloc_calls.load()); }
+
+tir_status tir_debug_hold_next_op(int32_t timeout_us) {
+    clear_error();
+    if (timeout_us <= 0) return fail(TIR_ERR_INVALID_ARG, "the hold needs a positive limit");
+    g_hold_next_op_us.store(timeout_us);
+    return TIR_OK;
+}
+
+tir_status tir_debug_hold_phase(tir_state* s, int32_t phase, int32_t timeout_us) {
+    clear_error();
+    if (!s || phase < 1 || phase >= s->n_phases || timeout_us <= 0)
+        return fail(TIR_ERR_INVALID_ARG, "hold needs a phase in [1, n_phases) and a positive limit");
+    s->hold_phase = phase;
+    s->hold_timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
+    return TIR_OK;
 }
 
 tir_status tir_attention(const float* q, const float* k_cache, const float* v_cache, float* out, int64_t q_heads,

@@ -433,6 +433,24 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int parts, int64
 // zeros, and no live row is gathered twice); then every sequence's device
 // length advances by its new tokens (every kernel of the forward that reads it
 // has run by now).
+// Layer outputs of the dumped rows: out[i] = X[rows[i]] + (Y's partial tiles
+// summed in order), the residual add the next rmsnorm kernel would do (Y null:
+// X as it is).
+__global__ void dump_rows_kernel(const float* __restrict__ X, const float* __restrict__ Y, int parts, int64_t part,
+                                 const int32_t* __restrict__ rows, int H, float* __restrict__ out) {
+    const int i = blockIdx.x;
+    const int64_t r = rows[i];
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+        float v = X[r * H + c];
+        if (Y) {
+            float y = Y[r * H + c];
+            for (int j = 1; j < parts; ++j) y += Y[j * part + r * H + c];
+            v += y;
+        }
+        out[static_cast<int64_t>(i) * H + c] = v;
+    }
+}
+
 __global__ void last_rows_kernel(int32_t* rows, Pages pg, int n_seqs) {
     griddep_launch_dependents();
     griddep_wait();
@@ -499,12 +517,20 @@ struct tir_batch {
     int32_t* gen = nullptr;  // generated ids [gen_cap][B] (tir_batch_generate)
     int gen_cap = 0;
     cudaGraphExec_t decode_graph = nullptr;  // one decode forward on `uni`, captured on first use
+    bool capturing = false;                  // forward() is being recorded into decode_graph
+    // tir_batch_dump_rows: per-layer outputs of chosen rows of the forwards
+    // run outside the decode graph, [n][layers][H] (rows in step-row order).
+    std::vector<int32_t> dump_rows;
+    float* dump = nullptr;
+    int32_t* dump_idx = nullptr;
     ~tir_batch() {
         cudaSetDevice(m ? m->device : 0);
         if (stream) cudaStreamSynchronize(stream);
         if (decode_graph) cudaGraphExecDestroy(decode_graph);
         if (gen) cudaFree(gen);
         if (logits) cudaFree(logits);
+        if (dump) cudaFree(dump);
+        if (dump_idx) cudaFree(dump_idx);
         for (void* p : allocs) cudaFree(p);
         if (h_next) cudaFreeHost(h_next);
         if (h_err) cudaFreeHost(h_err);
@@ -524,7 +550,7 @@ tir_status bfail(cudaError_t e, const char* what) {
 template <class T>
 bool balloc(tir_batch* b, size_t bytes, T** p) {
     void* q = nullptr;
-    if (cudaMalloc(&q, bytes ? bytes : 16) != cudaSuccess) return false;
+    if (dev_malloc(&q, bytes ? bytes : 16) != cudaSuccess) return false;
     b->allocs.push_back(q);
     *p = static_cast<T*>(q);
     return true;
@@ -552,7 +578,7 @@ tir_status mm(tir_batch* b, int64_t tokens, const tir_batch::GW& g, float* y, in
     const int splits = gemm_real_splits(g.k, gemm_splits(g.n, g.k, tokens, b->sms));
     if (splits > kMaxParts) return fail(TIR_ERR_UNSUPPORTED_SHAPE, "more split-K partial tiles than a reader sums");
     const int rc = launch_gemm_q8(g.w, g.p2, b->planes, b->inv, g.n, g.k, tokens, y, g.n, splits, b->err,
-                                  2000ull * 1000000ull, b->stream, true);
+                                  timeout_ns(), b->stream, true);
     if (rc != 0) return bfail(static_cast<cudaError_t>(rc), "tensor-core matmul");
     *parts = splits;
     return TIR_OK;
@@ -619,7 +645,15 @@ tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
     launch_kernel(embed_rows_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->ids, m->embd.q,
                   m->embd.s, m->embd.sk, H, V, b->X, b->err);
     int parts = 0, y_parts = 0;  // partial tiles of the latest matmul / of the one in Y
+    const int n_dump = b->capturing ? 0 : static_cast<int>(b->dump_rows.size());
+    auto dump_layer = [&](int l, const float* Y, int y_p) {  // output of layer l (0-based)
+        dump_rows_kernel<<<n_dump, 256, 0, st>>>(b->X, Y, y_p, T * H, b->dump_idx, H,
+                                                 b->dump + static_cast<size_t>(l) * n_dump * H);
+    };
+    for (int i = 0; i < n_dump; ++i)
+        if (b->dump_rows[static_cast<size_t>(i)] >= T) return fail(TIR_ERR_INVALID_ARG, "a dumped row is past the step's rows");
     for (int l = 0; l < L; ++l) {
+        if (n_dump > 0 && l > 0) dump_layer(l - 1, b->Y, y_parts);
         // the residual add of the previous layer's down projection (none before layer 0)
         if ((rc = planes_rc(launch_gemm_norm_planes(b->X, l > 0 ? b->Y : nullptr, y_parts, T * H, nullptr, T, H,
                                                     m->attn_norm[l], 1e-5f, b->planes, b->inv, st, true))) != TIR_OK)
@@ -648,6 +682,7 @@ tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
             return rc;
         if ((rc = mm(b, T, b->down[l], b->Y, &y_parts)) != TIR_OK) return rc;
     }
+    if (n_dump > 0 && L > 0) dump_layer(L - 1, b->Y, y_parts);
     launch_kernel(last_rows_kernel, dim3((b->B + 127) / 128), dim3(128), 0, st, true, b->rows, pg, b->B);
     // the last down projection's residual add, on the rows the logits need
     if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, y_parts, T * H, b->rows, b->B, H, m->out_norm, 1e-5f,
@@ -718,7 +753,9 @@ tir_status decode_forward(tir_batch* b) {
         cudaGraph_t g = nullptr;
         cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return bfail(e, "decode graph capture");
+        b->capturing = true;
         const tir_status rc = forward(b, b->uni, b->B, 1);
+        b->capturing = false;
         e = cudaStreamEndCapture(b->stream, &g);
         if (rc != TIR_OK) {
             if (g) cudaGraphDestroy(g);
@@ -865,10 +902,10 @@ tir_status tir_batch_create_paged(tir_model* m, int32_t n_seqs, int32_t max_ctx,
               balloc(b, static_cast<size_t>(gemm_tokens_padded(T)) * 4, &b->inv) && balloc(b, T * 4, &b->ids) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->rows) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->next) && balloc(b, 16, &b->err);
-    if (!ok || cudaMallocHost(&b->h_next, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
-        cudaMallocHost(&b->h_err, 16) != cudaSuccess ||
-        cudaMallocHost(&b->h_table, static_cast<size_t>(n_seqs) * b->max_pages * 4) != cudaSuccess ||
-        cudaMallocHost(&b->h_dyn, static_cast<size_t>(2 * n_seqs + T) * 4) != cudaSuccess) {
+    if (!ok || host_malloc_pinned(&b->h_next, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
+        host_malloc_pinned(&b->h_err, 16) != cudaSuccess ||
+        host_malloc_pinned(&b->h_table, static_cast<size_t>(n_seqs) * b->max_pages * 4) != cudaSuccess ||
+        host_malloc_pinned(&b->h_dyn, static_cast<size_t>(2 * n_seqs + T) * 4) != cudaSuccess) {
         delete b;
         return fail(TIR_ERR_OOM, "batch allocation failed");
     }
@@ -893,7 +930,7 @@ tir_status tir_batch_create_paged(tir_model* m, int32_t n_seqs, int32_t max_ctx,
     // tensor-core copies of every projection (through one block staging buffer)
     uint8_t* staging = nullptr;
     const size_t sbytes = static_cast<size_t>(std::max(m->lm.n * (m->lm.k / 32), m->gu[0].n * (m->gu[0].k / 32))) * 34;
-    if (cudaMalloc(&staging, sbytes) != cudaSuccess) {
+    if (dev_malloc(&staging, sbytes) != cudaSuccess) {
         delete b;
         return fail(TIR_ERR_OOM, "staging allocation failed");
     }
@@ -1024,6 +1061,48 @@ tir_status tir_batch_step(tir_batch* b, const int32_t* ids_host, int32_t tokens_
     return rc;
 }
 
+#define CUDA_BTRY(expr, what)                         \
+    do {                                              \
+        cudaError_t e_ = (expr);                      \
+        if (e_ != cudaSuccess) return bfail(e_, what); \
+    } while (0)
+
+tir_status tir_batch_dump_rows(tir_batch* b, const int32_t* rows_host, int32_t n_rows) {
+    clear_error();
+    if (!b || n_rows < 0 || (n_rows > 0 && !rows_host)) return fail(TIR_ERR_INVALID_ARG, "bad dump request");
+    cudaSetDevice(b->m->device);
+    cudaStreamSynchronize(b->stream);
+    if (b->dump) cudaFree(b->dump);
+    if (b->dump_idx) cudaFree(b->dump_idx);
+    b->dump = nullptr;
+    b->dump_idx = nullptr;
+    b->dump_rows.assign(rows_host, rows_host + n_rows);
+    if (n_rows == 0) return TIR_OK;
+    const int64_t T = static_cast<int64_t>(b->B) * b->max_tps;
+    for (int32_t r : b->dump_rows)
+        if (r < 0 || r >= T) {
+            b->dump_rows.clear();
+            return fail(TIR_ERR_INVALID_ARG, "dump row out of range");
+        }
+    const size_t bytes = static_cast<size_t>(n_rows) * b->m->t.layers * b->m->t.embed_dim * 4;
+    if (dev_malloc(&b->dump, bytes) != cudaSuccess || dev_malloc(&b->dump_idx, static_cast<size_t>(n_rows) * 4) != cudaSuccess) {
+        b->dump_rows.clear();
+        return fail(TIR_ERR_OOM, "dump allocation failed");
+    }
+    CUDA_BTRY(cudaMemset(b->dump, 0, bytes), "dump reset");
+    CUDA_BTRY(cudaMemcpy(b->dump_idx, rows_host, static_cast<size_t>(n_rows) * 4, cudaMemcpyHostToDevice), "dump rows");
+    return TIR_OK;
+}
+
+tir_status tir_batch_dump(tir_batch* b, float* out_host) {
+    clear_error();
+    if (!b || !out_host || b->dump_rows.empty()) return fail(TIR_ERR_INVALID_ARG, "no dump armed (tir_batch_dump_rows)");
+    cudaSetDevice(b->m->device);
+    const size_t bytes = b->dump_rows.size() * b->m->t.layers * b->m->t.embed_dim * 4;
+    CUDA_BTRY(cudaMemcpyAsync(out_host, b->dump, bytes, cudaMemcpyDeviceToHost, b->stream), "dump readback");
+    return check_err(b);
+}
+
 // Logits [n_seqs][vocab] of every sequence's last row in the last forward
 // (what src/forward.rs:242-252 returns per sequence; a sequence that took no
 // token in that step gets zeros): the lm_head partial tiles summed in order.
@@ -1033,7 +1112,7 @@ tir_status tir_batch_logits(tir_batch* b, float* logits_host) {
     if (b->lm_parts == 0) return fail(TIR_ERR_INVALID_ARG, "no forward has run on this batch");
     cudaSetDevice(b->m->device);
     const int64_t n = static_cast<int64_t>(b->B) * static_cast<int64_t>(b->m->t.vocab);
-    if (!b->logits && cudaMalloc(reinterpret_cast<void**>(&b->logits), static_cast<size_t>(n) * 4) != cudaSuccess)
+    if (!b->logits && dev_malloc(reinterpret_cast<void**>(&b->logits), static_cast<size_t>(n) * 4) != cudaSuccess)
         return fail(TIR_ERR_OOM, "logits allocation failed");
     int e = launch_gemm_sum_parts(b->LG, b->lm_parts, n, n, b->logits, b->stream, false);
     if (e != 0) return bfail(static_cast<cudaError_t>(e), "logits sum");
@@ -1065,7 +1144,7 @@ tir_status tir_batch_generate(tir_batch* b, const int32_t* prompts_host, int32_t
         if (b->gen) cudaFree(b->gen);
         b->gen = nullptr;
         b->gen_cap = 0;
-        if (cudaMalloc(reinterpret_cast<void**>(&b->gen), static_cast<size_t>(cap) * b->B * 4) != cudaSuccess)
+        if (dev_malloc(reinterpret_cast<void**>(&b->gen), static_cast<size_t>(cap) * b->B * 4) != cudaSuccess)
             return fail(TIR_ERR_OOM, "output allocation failed");
         b->gen_cap = cap;
     }

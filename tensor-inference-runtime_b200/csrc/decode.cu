@@ -127,10 +127,14 @@ __device__ __forceinline__ unsigned long long pack_best(float v, int idx) {
     return (static_cast<unsigned long long>(total_key(v)) << 32) | static_cast<uint32_t>(idx);
 }
 
+// error[0..2]: the launch's first failure (code, phase, step), which makes
+// every other wait give up; error[3]: the same code, left set for the host to
+// collect (the launcher clears only words 0..2 before a launch).
 __device__ __forceinline__ void set_error(const DecodeParams& p, uint32_t code, int ph, int f) {
     if (atomicCAS(p.error, 0u, code) == 0u) {
         p.error[1] = static_cast<uint32_t>(ph);
         p.error[2] = static_cast<uint32_t>(f);
+        p.error[3] = code;
     }
 }
 
@@ -1057,10 +1061,18 @@ __device__ __forceinline__ void run(const DecodeParams& p, Smem& s, Stream& sw) 
                 int ok = 1;
                 if (tid == 0) {
                     const uint64_t w0 = tr.on ? globaltimer_ns() : 0;
+                    // hold_phase (tests only) waits for one release more than
+                    // the grid makes, so that wait runs into its time limit
                     if (ph > 0)
-                        ok = wait_counter(p, p.counters + ph - 1, static_cast<uint32_t>((f + 1) * G), ph, f) ? 1 : 0;
+                        ok = wait_counter(p, p.counters + ph - 1,
+                                          static_cast<uint32_t>((f + 1) * G + (ph == p.hold_phase ? 1 : 0)), ph, f)
+                                 ? 1
+                                 : 0;
                     else if (f > 0)
-                        ok = wait_counter(p, p.counters + p.n_phases - 1, static_cast<uint32_t>(f * G), ph, f) ? 1 : 0;
+                        ok = wait_counter(p, p.counters + p.n_phases - 1,
+                                          static_cast<uint32_t>(f * G + (p.hold_phase == 0 ? 1 : 0)), ph, f)
+                                 ? 1
+                                 : 0;
                     if (tr.on) tr.dep_wait_ns += globaltimer_ns() - w0;
                 }
                 ok = __shfl_sync(FULL, ok, 0);

@@ -136,7 +136,7 @@ __device__ __forceinline__ bool gwait(const GemmParams& p, uint64_t* bar, uint32
         if ((n & 63u) == 63u) {
             if (ld_relaxed_gpu(p.err) != 0u) return false;
             if (globaltimer_ns() - t0 > p.timeout_ns) {
-                atomicCAS(p.err, 0u, kGErrTimeout);
+                if (atomicCAS(p.err, 0u, kGErrTimeout) == 0u) p.err[3] = kGErrTimeout;  // [3]: left for the host
                 return false;
             }
         }

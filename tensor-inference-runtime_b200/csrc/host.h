@@ -1,5 +1,7 @@
 // host.h -- host-side internals shared by the C ABI implementation files.
 #pragma once
+#include <cuda_runtime.h>
+
 #include <cstddef>
 #include <cstdint>
 #include <string>
@@ -13,6 +15,27 @@ namespace tir {
 // Thread-local error reporting (tir_last_error).
 tir_status fail(tir_status st, const std::string& msg);
 void clear_error();
+
+// Limit of every bounded device-side wait: TIR_TIMEOUT_MS (default 2000 ms).
+unsigned long long timeout_ns();
+
+// The library's allocation calls (counted; failable on demand for tests,
+// tir_debug_fail_alloc_after).
+cudaError_t dev_malloc(void** p, size_t bytes);
+cudaError_t dev_malloc_async(void** p, size_t bytes, cudaStream_t stream);
+cudaError_t host_malloc_pinned(void** p, size_t bytes);
+template <typename T>
+cudaError_t dev_malloc(T** p, size_t bytes) {
+    return dev_malloc(reinterpret_cast<void**>(p), bytes);
+}
+template <typename T>
+cudaError_t host_malloc_pinned(T** p, size_t bytes) {
+    return host_malloc_pinned(reinterpret_cast<void**>(p), bytes);
+}
+
+// The sticky error word of tir_swiglu_static's control block on `device`
+// (0: none), cleared by the read.  Makes no allocation.
+tir_status static_scratch_take_error(int device, uint32_t* code);
 
 // ---- GGUF (src/state.rs, src/reader.rs) ------------------------------------
 struct MetaValue {

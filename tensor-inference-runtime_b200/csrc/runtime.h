@@ -123,8 +123,9 @@ struct DecodeParams {
     const float* q;            // [H] (written by EPI_QKV)
     uint32_t* counters;        // [n_phases]
     unsigned long long* argmax_part;  // [grid]
-    uint32_t* error;           // [0] code, [1] phase, [2] step
+    uint32_t* error;           // [0] code, [1] phase, [2] step, [3] code again (sticky, read by the host)
     unsigned long long timeout_ns;
+    int32_t hold_phase;        // tests only: this phase's dependency is never met (-1: none)
     // Phase timeline of step `trace_step` (globaltimer ns), NULL when off:
     // trace[(phase * grid + cta) * kTraceFields + {0 start, 1 inputs ready,
     // 2 staged, 3 released, 4 ns waiting for ring data, 5 tiles, 6 ns waiting

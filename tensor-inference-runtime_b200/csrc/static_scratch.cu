@@ -28,8 +28,9 @@ constexpr int64_t kSwigluStaticMaxF = kMaxK;  // 6144
 // before being read on every call: no initial value needed.
 static __device__ __align__(256) float g_swiglu_scratch[3 * kSwigluStaticMaxF];
 // [0] phase counter (only ever incremented, any start value works);
-// [4..7] error words: must be zero when a matvec starts, so every call
-// clears them on its stream before its first launch.
+// [4..6] error words: must be zero when a matvec starts, so every call
+// clears them on its stream before its first launch; [7] the code of a
+// failed wait, kept until tir_ops_check collects it.
 static __device__ __align__(256) uint32_t g_swiglu_ctl[8];
 
 namespace {
@@ -86,7 +87,8 @@ tir_status matvec(const float* x, const uint8_t* quants, const uint16_t* scales,
     p.counters = ctl;
     p.error = ctl + 4;
     p.argmax_part = nullptr;  // EPI_STORE phases never touch it
-    p.timeout_ns = 2000ull * 1000000ull;
+    p.timeout_ns = timeout_ns();
+    p.hold_phase = -1;
     const int grid = d.n_tiles < sms ? d.n_tiles : sms;
     const int rc = decode_launch(p, grid, stream, false);
     if (rc != 0)
@@ -96,6 +98,19 @@ tir_status matvec(const float* x, const uint8_t* quants, const uint16_t* scales,
 }
 
 }  // namespace
+
+tir_status static_scratch_take_error(int device, uint32_t* code) {
+    *code = 0;
+    StaticBufs b;
+    const tir_status rc = static_bufs(device, &b);
+    if (rc != TIR_OK) return rc;
+    cudaError_t e = cudaMemcpy(code, b.ctl + 7, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && *code != 0u) e = cudaMemset(b.ctl + 7, 0, sizeof(uint32_t));
+    if (e != cudaSuccess)
+        return fail(TIR_ERR_CUDA, std::string("tir_swiglu_static: error word readback: ") + cudaGetErrorName(e));
+    return TIR_OK;
+}
+
 }  // namespace tir
 
 using namespace tir;
@@ -120,7 +135,7 @@ extern "C" tir_status tir_swiglu_static(const float* x, const uint8_t* gate_q, c
     const int sms = decode_grid_size(dev);
     if (sms <= 0) return fail(TIR_ERR_CUDA, "tir_swiglu_static: no multiprocessor count for the current device");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    e = cudaMemsetAsync(b.ctl + 4, 0, 4 * sizeof(uint32_t), st);
+    e = cudaMemsetAsync(b.ctl + 4, 0, 3 * sizeof(uint32_t), st);
     if (e != cudaSuccess) return fail(TIR_ERR_CUDA, std::string("tir_swiglu_static: clear error words: ") + cudaGetErrorName(e));
     float* gate = b.scratch;
     float* up = b.scratch + kSwigluStaticMaxF;

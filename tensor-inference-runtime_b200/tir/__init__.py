@@ -141,6 +141,8 @@ SIGNATURES = {
     "tir_batch_step": (C.c_int, [_vp, _vp, C.c_int32, _vp]),
     "tir_batch_generate": (C.c_int, [_vp, _vp, C.c_int32, C.c_int32, _vp]),
     "tir_batch_logits": (C.c_int, [_vp, _vp]),
+    "tir_batch_dump_rows": (C.c_int, [_vp, _vp, C.c_int32]),
+    "tir_batch_dump": (C.c_int, [_vp, _vp]),
     "tir_q8_gemm_bytes": (_i64, [_i64, _i64]),
     "tir_q8_gemm_rows": (_i64, [_i64]),
     "tir_q8_gemm_prepare": (C.c_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
@@ -153,6 +155,11 @@ SIGNATURES = {
     "tir_q8_act_matmul": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "tir_argmax": (C.c_int, [_vp, _i64, _vp, _vp]),
     "tir_attention": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "tir_ops_check": (C.c_int, [_vp]),
+    "tir_debug_fail_alloc_after": (None, [_i64]),
+    "tir_debug_alloc_count": (_i64, []),
+    "tir_debug_hold_phase": (C.c_int, [_vp, C.c_int32, C.c_int32]),
+    "tir_debug_hold_next_op": (C.c_int, [C.c_int32]),
 }
 
 _lib = None
@@ -520,6 +527,11 @@ class State:
     def enable_trace(self, step):
         check(lib().tir_state_enable_trace(self._h, int(step)))
 
+    def hold_phase(self, phase, timeout_us):
+        """Test hook: the next launch's wait at `phase` is never met and runs
+        out after timeout_us (the launch then returns TIR_ERR_TIMEOUT)."""
+        check(lib().tir_debug_hold_phase(self._h, int(phase), int(timeout_us)))
+
     def trace(self):
         """[n_phases, grid, 8]: stamps (ns) start/ready/staged/released, ns waiting
         for ring data, tiles, ns waiting for the previous phase."""
@@ -640,6 +652,19 @@ class Batch:
         check(lib().tir_batch_logits(self._h, out.ctypes.data))
         return out
 
+    def dump_rows(self, rows):
+        """Arms the per-layer dump of step rows `rows` (sequence-major indices)
+        for later forwards outside the decode graph (prefill, ragged steps)."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        check(lib().tir_batch_dump_rows(self._h, rows.ctypes.data if rows.size else None, rows.size))
+        self._dump_n = int(rows.size)
+
+    def dump(self):
+        """[n_rows, layers, embed_dim]: the armed rows' layer outputs of the last such forward."""
+        out = np.empty((self._dump_n, self.model.info["layers"], self.model.info["embed_dim"]), np.float32)
+        check(lib().tir_batch_dump(self._h, out.ctypes.data))
+        return out
+
 
 def q8_gemm_prepare(blocks, n, k, stream=None):
     """Tensor-core layout of a Q8_0 [n][k] matrix from device blocks: (w, w_pow2)."""
@@ -709,6 +734,28 @@ def swiglu_static(x, gate, up, down, out, k, f, stream=None):
     allocates no device memory.  Calls on one device must not overlap."""
     check(lib().tir_swiglu_static(_ptr(x), _ptr(gate[0]), _ptr(gate[1]), _ptr(up[0]), _ptr(up[1]),
                                   _ptr(down[0]), _ptr(down[1]), _ptr(out), k, f, _stream(stream)))
+
+
+def ops_check(stream=None):
+    """Synchronises `stream`; raises TirError(TIMEOUT) if an op launched on the
+    current device since the last check had a device-side wait give up."""
+    check(lib().tir_ops_check(_stream(stream)))
+
+
+def fail_alloc_after(n):
+    """Test hook: the n-th next allocation of the library fails once (n < 0: off)."""
+    lib().tir_debug_fail_alloc_after(int(n))
+
+
+def hold_next_op(timeout_us):
+    """Test hook: the next streaming matvec runs a held second pass that gives
+    up after timeout_us (reported by ops_check)."""
+    check(lib().tir_debug_hold_next_op(int(timeout_us)))
+
+
+def alloc_count():
+    """Allocation calls the library has made so far (device, async, pinned)."""
+    return int(lib().tir_debug_alloc_count())
 
 
 def activated_q8(x, k, out_blocks, stream=None):

@@ -28,8 +28,13 @@ def kat():
 
 @pytest.fixture(scope="session")
 def orc():
+    """The oracle in its fast mode (eight rows per pass, attention heads in
+    parallel): the same bits as the reference's loop order, which
+    tests/test_oracle_kat.py checks."""
     from oracle import load_oracle
-    return load_oracle()
+    o = load_oracle()
+    o.set_fast(True)
+    return o
 
 
 @pytest.fixture(scope="session")

@@ -3,9 +3,10 @@
 Reads the unit tests of ZeroR0R/tensor-inference-runtime as text (they are the
 only golden vectors the reference has for this path; its golden-token tests
 need a model file that is not distributed) and writes the arrays and expected
-values they assert.  Run from the repo root with the reference checked out:
+values they assert.  Run from the repo root, giving the directory of a checkout
+of the reference crate:
 
-    python tests/golden/extract_kat.py /root/reference
+    python tests/golden/extract_kat.py REFERENCE_CHECKOUT
 
 The tests read the committed JSON; nothing reads the reference at test time.
 """
@@ -121,4 +122,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: extract_kat.py REFERENCE_CHECKOUT  (the reference crate's root directory)")
+    main(sys.argv[1])

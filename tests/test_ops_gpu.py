@@ -355,8 +355,9 @@ def test_swiglu(cuda, tirlib, orc):
 @pytest.mark.parametrize("tokens,k,n", [(64, 2048, 2560), (300, 2048, 2048), (128, 5632, 2048), (7, 128, 7),
                                         (1, 2048, 32000), (257, 1024, 130), (64, 2048, 11264), (33, 5632, 2048)])
 def test_q8_matmul_batch_vs_oracle(cuda, tirlib, orc, tokens, k, n):
-    """Tensor-core batched matmul (3-pass f16 split, f32 accumulation) against
-    the oracle's q8_matmul token by token: rel-L2 below 1e-5 per token."""
+    """Tensor-core batched matmul (3-pass f16 split, f32 accumulation): every
+    token row against the float64 product of the dequantised weights, and
+    three rows against the oracle's q8_matmul; rel-L2 below 1e-5 per row."""
     torch = cuda
     rng = np.random.default_rng(tokens + k + n)
     _, blocks = synth.gemv_case(k, n, seed=k * 3 + n)
@@ -366,6 +367,13 @@ def test_q8_matmul_batch_vs_oracle(cuda, tirlib, orc, tokens, k, n):
     y = torch.empty(tokens * n, dtype=torch.float32, device="cuda")
     tirlib.q8_matmul_batch(dev(torch, x), tokens, w, y, n, k)
     got = host(y).reshape(tokens, n)
+    bl = blocks.reshape(n, k // 32, 34)
+    scale = bl[..., :2].copy().view(np.float16).astype(np.float64)      # [n, k/32, 1]
+    w64 = (bl[..., 2:].view(np.int8).astype(np.float64) * scale).reshape(n, k)
+    dense = x.astype(np.float64) @ w64.T                                # [tokens, n]
+    del w64
+    err = np.linalg.norm(got.astype(np.float64) - dense, axis=1) / np.maximum(np.linalg.norm(dense, axis=1), 1e-30)
+    assert err.max() < 1e-5, (int(err.argmax()), float(err.max()))
     for t in sorted({0, tokens // 2, tokens - 1}):
         ref = orc.q8_matmul(x[t], blocks.reshape(-1), n)
         assert rel_l2(got[t], ref) < 1e-5, t

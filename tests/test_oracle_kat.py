@@ -160,3 +160,24 @@ def test_q8_act_matmul_integer_block_dot(orc):
             sb = np.float32(wb[:2].view(np.float16)[0])
             total = np.float32(total + np.float32(np.float32(np.float32(isum) * sa) * sb))
         assert out[r] == total
+
+
+def test_fast_mode_is_bit_identical(orc, small_path):
+    """The tests run the oracle in its fast mode (eight matrix rows per pass,
+    attention heads in parallel); every row and head keeps the reference's
+    operation order, so its forward must equal the reference-order forward bit
+    for bit, including a q8_matmul whose row count is not a multiple of 8."""
+    from oracle.gguf_ref import GGUF
+    from tir import synth
+    x, blocks = synth.gemv_case(1024, 203, seed=4)
+    outs = {}
+    for fast in (False, True):
+        orc.set_fast(fast)
+        om = orc.model(GGUF(small_path))
+        steps = [om.forward(om.embed(t), p, dump=True) for p, t in enumerate([3, 77, 1500, 9])]
+        outs[fast] = (steps, orc.q8_matmul(x, blocks.reshape(-1), 203))
+    orc.set_fast(True)
+    for (la, da), (lb, db) in zip(outs[False][0], outs[True][0]):
+        np.testing.assert_array_equal(la, lb)
+        np.testing.assert_array_equal(da, db)
+    np.testing.assert_array_equal(outs[False][1], outs[True][1])

@@ -40,8 +40,14 @@ def test_swiglu_static_matches_swiglu_twice(cuda, tirlib, orc, k, f):
         (x, wg, wu, wd), (dx, g, u, d) = _ffn(torch, tirlib, k, f, seed)
         want = torch.empty(k, dtype=torch.float32, device="cuda")
         got = torch.full((k,), float("nan"), dtype=torch.float32, device="cuda")
+        n0 = tirlib.alloc_count()
         tirlib.swiglu(dx, g, u, d, want, k, f)
+        n1 = tirlib.alloc_count()
         tirlib.swiglu_static(dx, g, u, d, got, k, f)
+        # the library's allocation counter sees tir_swiglu's per-call scratch
+        # and nothing from the static entry
+        assert n1 == n0 + 1 and tirlib.alloc_count() == n1
+        tirlib.ops_check()  # no device-side wait gave up
         torch.cuda.synchronize()
         calls.append((got.cpu().numpy(), want.cpu().numpy(), orc.swiglu(x, wg.reshape(-1), wu.reshape(-1),
                                                                           wd.reshape(-1), f)))
