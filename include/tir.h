@@ -410,10 +410,12 @@ tir_status tir_ops_check(void *stream);
  * state/batch creation (the reference's ModelLoadError, src/error.rs:49-59,
  * covers the same load step).  n < 0 disarms.
  * tir_debug_alloc_count: allocations attempted so far (all kinds).
- * tir_debug_hold_phase(s, phase, timeout_us): the next decode launch of `s`
- * waits for one release more than the grid makes at `phase` (>= 1) with a
- * limit of timeout_us, so that wait runs out on purpose: the launch returns
- * TIR_ERR_TIMEOUT and resets the state, whose next call decodes normally.
+ * tir_debug_hold_phase(s, phase, timeout_us): in the next decode launch of
+ * `s`, the dependency wait at the start of `phase` (in [0, n_phases); phase 0
+ * waits from the launch's second step on) expects one release more than the
+ * grid makes, with a limit of timeout_us, so that wait runs out on purpose:
+ * the launch returns TIR_ERR_TIMEOUT and resets the state, whose next call
+ * decodes normally.
  * tir_debug_hold_next_op(timeout_us): the next streaming Q8_0 matvec
  * (tir_q8_matmul, _qact, _tiled, or one inside tir_swiglu) completes its
  * output, then runs a second pass whose start waits for a release that never

@@ -195,10 +195,13 @@ tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_
     p.hold_phase = -1;
     if (const int us = g_hold_next_op_us.exchange(0); us > 0) {
         // a second pass of the same matvec whose start waits for one release
-        // more than the grid makes: it gives up after `us` and records it
+        // more than the grid makes (the counter, otherwise only ever
+        // incremented, starts from zero): it gives up after `us` and records it
         p.n_steps = 2;
         p.hold_phase = 0;
         p.timeout_ns = static_cast<unsigned long long>(us) * 1000ull;
+        CUDA_TRY(cudaMemsetAsync(c->counters, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream)),
+                 "counter reset");
     }
     const int grid = d.n_tiles < sms ? d.n_tiles : sms;
     CUDA_TRY(clear_launch_error(c->error, stream), "error reset");
@@ -1335,8 +1338,8 @@ tir_status tir_debug_hold_next_op(int32_t timeout_us) {
 
 tir_status tir_debug_hold_phase(tir_state* s, int32_t phase, int32_t timeout_us) {
     clear_error();
-    if (!s || phase < 1 || phase >= s->n_phases || timeout_us <= 0)
-        return fail(TIR_ERR_INVALID_ARG, "hold needs a phase in [1, n_phases) and a positive limit");
+    if (!s || phase < 0 || phase >= s->n_phases || timeout_us <= 0)
+        return fail(TIR_ERR_INVALID_ARG, "hold needs a phase in [0, n_phases) and a positive limit");
     s->hold_phase = phase;
     s->hold_timeout_ns = static_cast<unsigned long long>(timeout_us) * 1000ull;
     return TIR_OK;

@@ -437,7 +437,7 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int parts, int64
 // summed in order), the residual add the next rmsnorm kernel would do (Y null:
 // X as it is).
 __global__ void dump_rows_kernel(const float* __restrict__ X, const float* __restrict__ Y, int parts, int64_t part,
-                                 const int32_t* __restrict__ rows, int H, float* __restrict__ out) {
+                                 const int32_t* __restrict__ rows, int H, float* __restrict__ out, int64_t out_ld) {
     const int i = blockIdx.x;
     const int64_t r = rows[i];
     for (int c = threadIdx.x; c < H; c += blockDim.x) {
@@ -447,7 +447,7 @@ __global__ void dump_rows_kernel(const float* __restrict__ X, const float* __res
             for (int j = 1; j < parts; ++j) y += Y[j * part + r * H + c];
             v += y;
         }
-        out[static_cast<int64_t>(i) * H + c] = v;
+        out[static_cast<int64_t>(i) * out_ld + c] = v;
     }
 }
 
@@ -646,9 +646,9 @@ tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
                   m->embd.s, m->embd.sk, H, V, b->X, b->err);
     int parts = 0, y_parts = 0;  // partial tiles of the latest matmul / of the one in Y
     const int n_dump = b->capturing ? 0 : static_cast<int>(b->dump_rows.size());
-    auto dump_layer = [&](int l, const float* Y, int y_p) {  // output of layer l (0-based)
+    auto dump_layer = [&](int l, const float* Y, int y_p) {  // output of layer l (0-based) into dump[row][l]
         dump_rows_kernel<<<n_dump, 256, 0, st>>>(b->X, Y, y_p, T * H, b->dump_idx, H,
-                                                 b->dump + static_cast<size_t>(l) * n_dump * H);
+                                                 b->dump + static_cast<size_t>(l) * H, static_cast<int64_t>(L) * H);
     };
     for (int i = 0; i < n_dump; ++i)
         if (b->dump_rows[static_cast<size_t>(i)] >= T) return fail(TIR_ERR_INVALID_ARG, "a dumped row is past the step's rows");

@@ -45,15 +45,16 @@ def test_decode_wait_runs_out_then_state_recovers(cuda, tirlib, tiny_path):
         for p, t in enumerate(ids):
             np.testing.assert_array_equal(st.forward(t, p), want[p])
         st.reset()
-    # a multi-step launch (generate_capped) held in its third step
-    st.hold_phase(2 * n_ph + 1, HOLD_US)
+    # a multi-step launch (generate_capped): phase 0 waits for the previous
+    # step from the second step on, so the hold ends the launch in step 1
+    st.hold_phase(0, HOLD_US)
     with pytest.raises(tirlib.TirError) as e:
         st.generate_capped(np.array(ids, np.int32), 4)
-    assert e.value.name == "TIMEOUT" and "step 2" in str(e.value)
+    assert e.value.name == "TIMEOUT" and "phase 0, step 1" in str(e.value)
     np.testing.assert_array_equal(st.generate_capped(np.array(ids, np.int32), 4),
                                   ref.generate_capped(np.array(ids, np.int32), 4))
     with pytest.raises(tirlib.TirError) as e:
-        st.hold_phase(0, HOLD_US)
+        st.hold_phase(n_ph, HOLD_US)
     assert e.value.name == "INVALID_ARG"
     st.close()
     ref.close()
