@@ -9,14 +9,26 @@ persistent-kernel launch.
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
+The default run also measures the other workloads of the same model, each in
+its own timed region, as sub-objects of the one JSON line: "long" (1792 prompt
+ids + 256 greedy steps, context 2048), "batched" (64 sequences per GPU x (128
+prompt ids + 128 greedy steps) on the tensor-core path), "prefill" (16 x 512
+prompt ids per GPU in one batched forward) and, on rank 0, "gemv" (the
+isolated Q8_0 GEMV sweep over the five projection shapes).  --sub off skips
+them; --workload NAME runs one of them alone as the headline.
+
 N > 1 runs under torchrun, one process per GPU; each GPU holds a full weight
-replica and decodes its own sequence (replicas, no collective on the data path;
-torch.distributed only brackets the timed region).  Rank 0 prints one JSON line.
+replica and decodes its own sequences (replicas, no collective on the data
+path; torch.distributed only brackets the timed regions).  Rank 0 prints one
+JSON line; every value is the aggregate over ranks (tokens of all ranks / the
+slowest rank's device time).
 
 --impl reference times the oracle -- the C restatement of the reference's
-Rayon CPU path -- on the host cores, on a bounded sample of the same workload.
+Rayon CPU path -- on the host cores of rank 0 only, on a bounded sample of
+the same workload (not scaled with N).
 """
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -37,12 +49,16 @@ WORKLOAD = ("TinyLlama-1.1B-shape Llama-2 decoder (22 layers, hidden 2048, 32/4 
 METRIC = "decode tok/s (batch 1)"
 
 
-def workload_name(args):
-    if args.prompt == 16 and args.decode == 128:
+def workload_name_for(n_prompt, n_decode):
+    if n_prompt == 16 and n_decode == 128:
         return WORKLOAD
     return WORKLOAD.replace("16-token seeded prompt + 128 steps (144 forwards per step)",
-                            f"{args.prompt}-token seeded prompt + {args.decode} steps "
-                            f"({args.prompt + args.decode} forwards per step)")
+                            f"{n_prompt}-token seeded prompt + {n_decode} steps "
+                            f"({n_prompt + n_decode} forwards per step)")
+
+
+def workload_name(args):
+    return workload_name_for(args.prompt, args.decode)
 
 
 def parse_args(argv=None):
@@ -61,6 +77,9 @@ def parse_args(argv=None):
                          "sweep over the TinyLlama projection shapes; batched: 64 sequences per GPU, 128 prompt "
                          "ids + 128 greedy steps each, on the tensor-core path; prefill: 16 sequences x 512 prompt "
                          "ids per GPU in one batched forward")
+    ap.add_argument("--sub", choices=["on", "off"], default="on",
+                    help="with the default decode workload: also measure the long, batched, prefill and GEMV "
+                         "workloads as sub-objects of the line")
     ap.add_argument("--timeline", metavar="FILE.md", default=None,
                     help="after the timed region, trace forward step 100 of one more generate "
                          "and write the per-phase timeline summary to FILE.md")
@@ -221,12 +240,14 @@ def run_reference(args, dist):
         om.generate_capped(sample_prompt, sample_cap)
     dt = (time.perf_counter() - t0) / args.steps
     value = (len(sample_prompt) + sample_cap) / dt
-    sample = f"{len(sample_prompt)} prompt ids + {sample_cap} greedy steps of the workload per step"
+    sample = (f"{len(sample_prompt)} prompt ids + {sample_cap} greedy steps of the workload per step (positions "
+              f"0-{len(sample_prompt) + sample_cap - 1}: at these context lengths the reference's per-token cost is "
+              f"flat, so the rate stands for the whole workload's); one process on rank 0's host, not scaled with N")
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0 weights and token ids)",
             "config": {"workload": workload_name(args), "batch": 1, "prompt_tokens": args.prompt,
-                       "decode_tokens": args.decode, "parallelism": "host cores"},
+                       "decode_tokens": args.decode, "parallelism": "host cores of rank 0 (one process at any N)"},
             "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": orc.get_threads(), "kind": "port",
                              "sample": sample},
@@ -283,8 +304,124 @@ def cpu_baseline_batched(args):
             "sample": sample}
 
 
+def decode_source_sha():
+    """First 16 hex digits of the sha256 of the decode kernel's sources: a
+    committed ncu traffic figure applies only to the build it was taken on."""
+    h = hashlib.sha256()
+    for name in ("decode.cu", "runtime.h", "ptx.cuh"):
+        with open(os.path.join(PKG, "csrc", name), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def committed_traffic(n_prompt, n_decode):
+    """DRAM bytes of one decode launch from profiles/decode_traffic.json when it
+    was taken on this workload and on these decode-kernel sources, else None."""
+    tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
+    if not os.path.exists(tpath):
+        return None, "no committed capture"
+    with open(tpath) as f:
+        t = json.load(f)
+    if t.get("prompt") != n_prompt or t.get("decode") != n_decode:
+        return None, "committed capture is of another workload"
+    if t.get("source_sha") != decode_source_sha():
+        return None, "committed capture is of another build of the decode kernel"
+    return t.get("bytes_per_launch"), "ncu capture of this build (profiles/decode_traffic.json)"
+
+
+def measure_decode(model, dist, n_prompt, n_decode, steps, warmup, seed, timeline=None):
+    """generate_capped of n_prompt seeded ids + n_decode greedy steps, one
+    launch per step: device time with the prompt resident in HBM (CUDA events
+    on the state's stream, max over ranks), then end to end through the host
+    API (host ids in and out).  Returns the JSON fields of the measurement."""
+    import torch
+
+    from tir import synth
+
+    dev = dist.local
+    info = model.info
+    n_fwd = n_prompt + n_decode
+    st = model.state(max_ctx=n_fwd)
+    stream = torch.cuda.ExternalStream(st.stream(), device=torch.device("cuda", dev))
+    # each rank decodes its own sequence (weak scaling)
+    prompt = synth.prompt_ids(n_prompt, info["vocab"], seed=decode_seed(seed, dist.rank))
+    d_prompt = torch.from_numpy(prompt.copy()).to(f"cuda:{dev}")
+    d_out = torch.empty(n_decode, dtype=torch.int32, device=f"cuda:{dev}")
+
+    def step():
+        st.generate_capped_device(d_prompt, n_prompt, n_decode, d_out)
+
+    for _ in range(warmup):
+        step()
+    st.sync()
+
+    props = torch.cuda.get_device_properties(dev)
+    uuid = str(getattr(props, "uuid", "")) or None
+    # ---- device-timed region (inputs resident in HBM) -----------------------
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(uuid) as clocks:
+        time.sleep(0.05)
+        ev[0].record(stream)
+        for i in range(steps):
+            step()
+            ev[i + 1].record(stream)
+        torch.cuda.synchronize(dev)
+    st.sync()
+    ms_local = sum(ev[i].elapsed_time(ev[i + 1]) for i in range(steps)) / steps
+    dist.barrier()
+    ms = dist.max(ms_local)
+
+    # ---- end to end through the host API (host ids in and out) -------------
+    for _ in range(max(1, warmup // 2)):
+        st.generate_capped(prompt, n_decode)
+    dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ids = st.generate_capped(prompt, n_decode)
+    torch.cuda.synchronize(dev)
+    e2e_local = (time.perf_counter() - t0) / steps * 1e3
+    dist.barrier()
+    e2e_ms = dist.max(e2e_local)
+    assert ids.shape == (n_decode,)
+
+    total_tokens = n_fwd * dist.world
+    peak, peak_kind = peaks()
+    alg = algorithmic_bytes(info, model.weight_bytes(), n_fwd)
+    achieved = alg / (ms_local / 1e3) / 1e9
+    traffic, traffic_src = committed_traffic(n_prompt, n_decode)
+    out = {
+        "value": total_tokens / (ms / 1e3), "unit": "tok/s", "steps": steps, "warmup": warmup, "ms_per_step": ms,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "traffic_source": traffic_src,
+                     "peak_kind": peak_kind, "kernel": "tir::decode_kernel (one launch per step)",
+                     "algorithmic_bytes_per_launch": alg},
+        "e2e": {"value": total_tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt,
+                "d2h_bytes_per_step": 4 * n_decode + 12},
+        "gpu_launches": steps,
+        "clocks": clocks.summary(),
+    }
+    if timeline and dist.rank == 0:
+        from tir import timeline as tl
+        st.enable_trace(min(100, n_fwd - 1))
+        st.generate_capped(prompt, n_decode)
+        st.enable_trace(-1)
+        with open(timeline, "w") as f:
+            f.write(tl.to_markdown(tl.summarize(st.trace())) + "\n")
+    st.close()
+    return out
+
+
+def decode_config(n_prompt, n_decode, world):
+    return {"workload": workload_name_for(n_prompt, n_decode), "batch": 1, "prompt_tokens": n_prompt,
+            "decode_tokens": n_decode, "forwards_per_step": n_prompt + n_decode,
+            "parallelism": f"replicas x{world} (no collective)",
+            "l2": "inputs larger than L2: 1.10 GB of weights streamed per forward vs 126 MB L2"}
+
+
 def run_ours(args, dist):
-    import numpy as np
     import torch
 
     import tir
@@ -295,96 +432,27 @@ def run_ours(args, dist):
     if dist.rank == 0:
         synth.synthetic_model("tinyllama", args.seed)
     dist.barrier()
-    path = synth.synthetic_model("tinyllama", args.seed)
-    model = tir.Model(path, device=dev)
-    info = model.info
-    n_fwd = args.prompt + args.decode
-    st = model.state(max_ctx=n_fwd)
-    stream = torch.cuda.ExternalStream(st.stream(), device=torch.device("cuda", dev))
-    # each rank decodes its own sequence (weak scaling)
-    prompt = synth.prompt_ids(args.prompt, info["vocab"], seed=decode_seed(args.seed, dist.rank))
-    d_prompt = torch.from_numpy(prompt.copy()).to(f"cuda:{dev}")
-    d_out = torch.empty(args.decode, dtype=torch.int32, device=f"cuda:{dev}")
-
-    def step():
-        st.generate_capped_device(d_prompt, args.prompt, args.decode, d_out)
-
-    for _ in range(args.warmup):
-        step()
-    st.sync()
-
-    props = torch.cuda.get_device_properties(dev)
-    uuid = str(getattr(props, "uuid", "")) or None
-    # ---- device-timed region (inputs resident in HBM) -----------------------
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(uuid) as clocks:
-        time.sleep(0.05)
-        ev[0].record(stream)
-        for i in range(args.steps):
-            step()
-            ev[i + 1].record(stream)
-        torch.cuda.synchronize(dev)
-    st.sync()
-    per_launch = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
-    ms_local = sum(per_launch) / args.steps
-    dist.barrier()
-    ms = dist.max(ms_local)
-
-    # ---- end to end through the host API (host ids in and out) -------------
-    for _ in range(max(1, args.warmup // 2)):
-        st.generate_capped(prompt, args.decode)
-    dist.barrier()
-    torch.cuda.synchronize(dev)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        ids = st.generate_capped(prompt, args.decode)
-    torch.cuda.synchronize(dev)
-    e2e_local = (time.perf_counter() - t0) / args.steps * 1e3
-    dist.barrier()
-    e2e_ms = dist.max(e2e_local)
-    assert ids.shape == (args.decode,)
-
-    total_tokens = n_fwd * dist.world
-    value = total_tokens / (ms / 1e3)
-    peak, peak_kind = peaks()
-    alg = algorithmic_bytes(info, model.weight_bytes(), n_fwd)
-    achieved = alg / (ms_local / 1e3) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "decode_traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as f:
-            t = json.load(f)
-        if t.get("prompt") == args.prompt and t.get("decode") == args.decode:
-            traffic = t.get("bytes_per_launch")
-    line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0 weights and token ids)",
-        "config": {"workload": workload_name(args), "batch": 1, "prompt_tokens": args.prompt,
-                   "decode_tokens": args.decode,
-                   "forwards_per_step": n_fwd, "parallelism": f"replicas x{dist.world} (no collective)",
-                   "l2": "inputs larger than L2: 1.10 GB of weights streamed per forward vs 126 MB L2"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "tir::decode_kernel (one launch per step)",
-                     "algorithmic_bytes_per_launch": alg},
-        "e2e": {"value": total_tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 4 * args.prompt,
-                "d2h_bytes_per_step": 4 * args.decode + 12},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-    }
+    model = tir.Model(synth.synthetic_model("tinyllama", args.seed), device=dev)
+    m = measure_decode(model, dist, args.prompt, args.decode, args.steps, args.warmup, args.seed, args.timeline)
+    line = {"metric": METRIC, "value": m["value"], "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0 weights and token ids)",
+            "config": decode_config(args.prompt, args.decode, dist.world)}
+    for k in ("roofline", "e2e", "gpu_launches", "clocks"):
+        line[k] = m[k]
     if dist.rank == 0 and dist.world == 1 and args.cpu_baseline == "auto":
         line["cpu_baseline"] = cpu_baseline(args)
-    if args.timeline and dist.rank == 0:
-        from tir import timeline
-        st.enable_trace(min(100, n_fwd - 1))
-        st.generate_capped(prompt, args.decode)
-        st.enable_trace(-1)
-        with open(args.timeline, "w") as f:
-            f.write(timeline.to_markdown(timeline.summarize(st.trace())) + "\n")
-    st.close()
+    if args.sub == "on" and args.workload == "decode" and (args.prompt, args.decode) == (16, 128):
+        # the other workloads of the same model, each in its own timed region
+        sub_steps, sub_warm = max(1, min(args.steps, 3)), max(3, min(args.warmup, 3))
+        long_m = measure_decode(model, dist, 1792, 256, sub_steps, sub_warm, args.seed)
+        line["long"] = dict(metric="decode tok/s (batch 1, context 2048)", config=decode_config(1792, 256, dist.world),
+                            **long_m)
+        for kind in ("batched", "prefill"):
+            line[kind] = measure_batched(model, dist, kind, 128, sub_steps, sub_warm, args.seed)
+        if dist.rank == 0:
+            line["gemv"] = measure_gemv(dev, sub_steps, sub_warm, args.seed)
+            line["gemv"]["ranks"] = "rank 0 only (a per-GPU figure)"
     model.close()
     return line
 
@@ -392,7 +460,7 @@ def run_ours(args, dist):
 GEMV_SHAPES = [(2048, 2048), (2048, 256), (2048, 5632), (5632, 2048), (2048, 32000)]  # (K, N)
 
 
-def run_gemv(args):
+def measure_gemv(dev, steps, warmup, seed):
     """Isolated Q8_0 GEMV sweep (batch 1) over the TinyLlama projection shapes:
     x f32 N(0, 1), weights int8 uniform in [-127, 127] with f16 scales
     |N(0, 0.02)| / 127, seeded, in the tile-major layout the decode kernel
@@ -402,8 +470,8 @@ def run_gemv(args):
     import torch
 
     import tir
-    torch.cuda.set_device(0)
-    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device="cuda").manual_seed(seed)
     l2 = 126 * 2 ** 20
     per_shape = []
     tot_bytes, tot_ms = 0.0, 0.0
@@ -424,9 +492,9 @@ def run_gemv(args):
             del q, sc, blocks
         x = torch.randn(k, device="cuda", generator=g)
         out = torch.empty(n, device="cuda")
-        for i in range(max(args.warmup, 3) * copies):
+        for i in range(max(warmup, 3) * copies):
             tir.q8_matmul_tiled(x, ws[i % copies], out, n, k)
-        iters = max(args.steps, 1) * copies
+        iters = max(steps, 1) * copies
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record(stream)
@@ -442,68 +510,67 @@ def run_gemv(args):
     peak, peak_kind = peaks()
     gbs = tot_bytes / (tot_ms / 1e3) / 1e9
     line = {"metric": "Q8_0 GEMV weight GB/s (batch 1, TinyLlama projection shapes)", "value": gbs, "unit": "GB/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms,
+            "n_gpus": 1, "steps": steps, "warmup": warmup, "ms_per_step": tot_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded int8 weights, f16 scales, f32 activations)",
             "config": {"workload": "Q8_0 GEMV sweep K->N: " + ", ".join(f"{k}->{n}" for k, n in GEMV_SHAPES),
                        "l2": "each launch reads the next of >= 4x L2 of weight copies"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
                          "traffic": None, "peak_kind": peak_kind},
-            "shapes": per_shape, "gpu_launches": sum(max(args.steps, 1) * s["copies"] for s in per_shape)}
-    print(json.dumps(line), flush=True)
+            "shapes": per_shape, "gpu_launches": sum(max(steps, 1) * s["copies"] for s in per_shape)}
+    return line
 
 
-def run_batched(args, dist):
+def run_gemv(args):
+    print(json.dumps(measure_gemv(0, args.steps, args.warmup, args.seed)), flush=True)
+
+
+def measure_batched(model, dist, kind, decode_cap, steps, warmup, seed, cpu=None):
     """Batched sequences on the tensor-core path (one process per GPU, weak
-    scaling).  batched: 64 sequences x (128 seeded prompt ids + 128 greedy
-    steps), value = all token forwards / device time of one generate; prefill:
-    16 sequences x 512 seeded ids in one batched forward, value = prompt
-    tokens / device time."""
+    scaling).  batched: 64 sequences x (128 seeded prompt ids + decode_cap
+    greedy steps), value = all token forwards / device time of one generate;
+    prefill: 16 sequences x 512 seeded ids in one batched forward, value =
+    prompt tokens / device time.  cpu: the arguments of the oracle's CPU
+    baseline for this workload (rank 0, N = 1), or None."""
     import numpy as np
     import torch
 
     import tir
-    from tir import synth
 
     dev = dist.local
-    torch.cuda.set_device(dev)
-    if dist.rank == 0:
-        synth.synthetic_model("tinyllama", args.seed)
-    dist.barrier()
-    model = tir.Model(synth.synthetic_model("tinyllama", args.seed), device=dev)
     info = model.info
     V = info["vocab"]
-    if args.workload == "batched":
-        B, P, cap = 64, 128, args.decode  # --decode shortens the run for profiling (default 128)
+    if kind == "batched":
+        B, P, cap = 64, 128, decode_cap
     else:
         B, P, cap = 16, 512, 0
-    rng = np.random.default_rng(batched_seed(args.seed, dist.rank))
+    rng = np.random.default_rng(batched_seed(seed, dist.rank))
     prompts = rng.integers(3, V, size=(B, P), dtype=np.int32)
     batch = tir.Batch(model, B, max_ctx=P + cap + 1, max_tokens_per_seq=P)
     stream = torch.cuda.ExternalStream(batch.stream(), device=torch.device("cuda", dev))
 
     def step():
-        if args.workload == "batched":
+        if kind == "batched":
             return batch.generate(prompts, cap)
         batch.reset()
         return batch.step(prompts)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     props = torch.cuda.get_device_properties(dev)
     uuid = str(getattr(props, "uuid", "")) or None
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     dist.barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(uuid) as clocks:
         t0 = time.perf_counter()  # after the sampler's start-up, which is not the workload's
         ev[0].record(stream)
-        for i in range(args.steps):
+        for i in range(steps):
             step()
             ev[i + 1].record(stream)
         torch.cuda.synchronize(dev)
-        wall_ms = (time.perf_counter() - t0) / args.steps * 1e3
-    ms_local = sum(ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)) / args.steps
+        wall_ms = (time.perf_counter() - t0) / steps * 1e3
+    ms_local = sum(ev[i].elapsed_time(ev[i + 1]) for i in range(steps)) / steps
     dist.barrier()
     ms = dist.max(ms_local)
     e2e_ms = dist.max(wall_ms)
@@ -517,7 +584,7 @@ def run_batched(args, dist):
     L_ = info["layers"]
     launches_per_step = (1 + 10 * L_ + 4) + cap * (1 + 9 * L_ + 4 + 1)
     wb = model.weight_bytes()
-    if args.workload == "batched":
+    if kind == "batched":
         name = (f"TinyLlama-1.1B-shape Q8_0 model, {B} sequences per GPU, each {P} seeded prompt ids (one batched "
                 f"prefill) + {cap} greedy steps in lockstep ({B * forwards} token forwards per step)")
         kv_pos = 2 * info["layers"] * info["kv_dim"] * 4
@@ -548,7 +615,7 @@ def run_batched(args, dist):
                 "algorithmic_flops_per_step": flops}
         metric = "prefill tok/s (16 x 512 tokens per GPU, aggregate)"
     line = {"metric": metric, "value": tokens / (ms / 1e3), "unit": "tok/s", "n_gpus": dist.world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 (3-pass f16 tensor cores, f32 accumulation)",
             "data": "synthetic (seeded Q8_0 weights and token ids)",
             "config": {"workload": name, "sequences_per_gpu": B, "prompt_tokens": P, "decode_tokens": cap,
@@ -557,11 +624,28 @@ def run_batched(args, dist):
             "roofline": roof,
             "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": B * P * 4,
                     "d2h_bytes_per_step": B * cap * 4 + 4},
-            "gpu_launches": args.steps * launches_per_step, "clocks": clocks.summary()}
+            "gpu_launches": steps * launches_per_step, "clocks": clocks.summary()}
     batch.close()
+    if cpu is not None and dist.world == 1:
+        line["cpu_baseline"] = cpu_baseline_batched(cpu)
+    return line
+
+
+def run_batched(args, dist):
+    import torch
+
+    import tir
+    from tir import synth
+
+    dev = dist.local
+    torch.cuda.set_device(dev)
+    if dist.rank == 0:
+        synth.synthetic_model("tinyllama", args.seed)
+    dist.barrier()
+    model = tir.Model(synth.synthetic_model("tinyllama", args.seed), device=dev)
+    line = measure_batched(model, dist, args.workload, args.decode, args.steps, args.warmup, args.seed,
+                           cpu=args if args.cpu_baseline == "auto" else None)
     model.close()
-    if args.cpu_baseline == "auto" and dist.world == 1:
-        line["cpu_baseline"] = cpu_baseline_batched(args)
     return line
 
 

@@ -37,3 +37,24 @@ def test_workload_arguments():
     b = bench.parse_args(["--workload", "long"])
     assert (b.prompt, b.decode) == (1792, 256)
     assert "1792-token seeded prompt + 256 steps (2048 forwards per step)" in bench.workload_name(b)
+
+
+def test_committed_traffic_follows_the_build(tmp_path, monkeypatch):
+    """A committed ncu traffic figure is used only on the decode-kernel build
+    (source hash) and workload it was captured on."""
+    import json
+    import os
+    sha = bench.decode_source_sha()
+    assert len(sha) == 16 and sha == bench.decode_source_sha()
+    prof = tmp_path / "profiles"
+    prof.mkdir()
+    monkeypatch.setattr(bench, "ROOT", str(tmp_path))
+    assert bench.committed_traffic(16, 128)[0] is None
+    rec = {"prompt": 16, "decode": 128, "bytes_per_launch": 123, "source_sha": sha}
+    (prof / "decode_traffic.json").write_text(json.dumps(rec))
+    assert bench.committed_traffic(16, 128)[0] == 123
+    assert bench.committed_traffic(1792, 256)[0] is None
+    rec["source_sha"] = "0" * 16
+    (prof / "decode_traffic.json").write_text(json.dumps(rec))
+    assert bench.committed_traffic(16, 128)[0] is None
+    assert os.path.exists(os.path.join(bench.PKG, "csrc", "decode.cu"))
