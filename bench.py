@@ -81,8 +81,10 @@ def parse_args(argv=None):
                     help="with the default decode workload: also measure the long, batched, prefill and GEMV "
                          "workloads as sub-objects of the line")
     ap.add_argument("--timeline", metavar="FILE.md", default=None,
-                    help="after the timed region, trace forward step 100 of one more generate "
-                         "and write the per-phase timeline summary to FILE.md")
+                    help="after the timed region, trace one forward step (--timeline-step) of one more "
+                         "generate and write the per-phase timeline summary to FILE.md")
+    ap.add_argument("--timeline-step", type=int, default=100,
+                    help="the traced forward step (0-based; clamped to the generate's last step)")
     args = ap.parse_args(argv)
     if args.workload == "long":
         args.prompt, args.decode = 1792, 256
@@ -329,7 +331,7 @@ def committed_traffic(n_prompt, n_decode):
     return t.get("bytes_per_launch"), "ncu capture of this build (profiles/decode_traffic.json)"
 
 
-def measure_decode(model, dist, n_prompt, n_decode, steps, warmup, seed, timeline=None):
+def measure_decode(model, dist, n_prompt, n_decode, steps, warmup, seed, timeline=None, timeline_step=100):
     """generate_capped of n_prompt seeded ids + n_decode greedy steps, one
     launch per step: device time with the prompt resident in HBM (CUDA events
     on the state's stream, max over ranks), then end to end through the host
@@ -405,7 +407,7 @@ def measure_decode(model, dist, n_prompt, n_decode, steps, warmup, seed, timelin
     }
     if timeline and dist.rank == 0:
         from tir import timeline as tl
-        st.enable_trace(min(100, n_fwd - 1))
+        st.enable_trace(min(max(timeline_step, 0), n_fwd - 1))
         st.generate_capped(prompt, n_decode)
         st.enable_trace(-1)
         with open(timeline, "w") as f:
@@ -433,7 +435,8 @@ def run_ours(args, dist):
         synth.synthetic_model("tinyllama", args.seed)
     dist.barrier()
     model = tir.Model(synth.synthetic_model("tinyllama", args.seed), device=dev)
-    m = measure_decode(model, dist, args.prompt, args.decode, args.steps, args.warmup, args.seed, args.timeline)
+    m = measure_decode(model, dist, args.prompt, args.decode, args.steps, args.warmup, args.seed, args.timeline,
+                       args.timeline_step)
     line = {"metric": METRIC, "value": m["value"], "unit": "tok/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": m["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Q8_0 weights and token ids)",

@@ -207,6 +207,13 @@ tir_status tir_state_enable_dump(tir_state *s, int32_t enable);
 tir_status tir_state_dump(tir_state *s, float *out_host);
 /* The layer outputs alone: layers x embed_dim floats (rows 1.. of the dump). */
 tir_status tir_debug_dump_layers(tir_state *s, float *out_host);
+/* Mode::Quantize: the Q8_0 blocks activated_q8 (src/kernels.rs:8-31) made of
+ * the q|k|v, o and lm_head inputs in the last forward, as the fused kernel
+ * staged them: [(2 L + 1)][embed_dim / 32] blocks of 34 bytes ([2 l] q|k|v of
+ * layer l, [2 l + 1] o of layer l, [2 L] lm_head).  Needs the dump on
+ * (tir_state_enable_dump) and the model in Mode 1; runtime extension for
+ * parity tests. */
+tir_status tir_debug_dump_qact(tir_state *s, uint8_t *out_host);
 /* Phase timeline (profiling; the reference's tracing is the debug-build
  * save_intermediate, src/forward.rs:287-308): with step >= 0, every later
  * launch records, for forward step `step`, eight values per phase per CTA:

@@ -67,6 +67,7 @@ class Oracle:
                                               C.c_size_t, C.c_size_t, _i32p, _f32p]),
             "orc_set_threads": (None, [C.c_int]),
             "orc_set_fast": (None, [C.c_int]),
+            "orc_set_attn_dump": (None, [C.c_void_p]),
             "orc_get_threads": (C.c_int, []),
         }
         for name, (res, args) in sig.items():
@@ -219,6 +220,17 @@ class OracleModel:
 
     def embed(self, id_):
         return self.orc.embed(id_, self._arrays[0], self.dims.embed_dim)
+
+    def forward_attn(self, token, pos):
+        """forward with the per-layer dump, plus each layer's attention output
+        (the output projection's input): (logits, dump, attn [L][H])."""
+        attn = np.empty((self.dims.n_layers, self.dims.embed_dim), np.float32)
+        self.orc.lib.orc_set_attn_dump(attn.ctypes.data)
+        try:
+            logits, dump = self.forward(token, pos, dump=True)
+        finally:
+            self.orc.lib.orc_set_attn_dump(None)
+        return logits, dump, attn
 
     def forward(self, token, pos, dump=False):
         d = self.dims

@@ -30,6 +30,12 @@ void orc_set_threads(int n) { g_threads = n; }
 
 void orc_set_fast(int on) { g_fast = on ? 1 : 0; }
 
+/* When set, orc_forward also copies each layer's attention output (the input
+ * of the output projection, src/forward.rs:176) to attn_dump + l * embed_dim. */
+static float *g_attn_dump = NULL;
+
+void orc_set_attn_dump(float *buf) { g_attn_dump = buf; }
+
 int orc_get_threads(void) {
 #ifdef _OPENMP
     return g_threads > 0 ? g_threads : omp_get_max_threads();
@@ -426,6 +432,7 @@ int orc_forward(const orc_dims *d, const void *const *T, orc_cache *cache,
             }
         }
 
+        if (g_attn_dump) memcpy(g_attn_dump + l * H, weighted_values, H * sizeof(float));
         /* :176-192 output projection and residual */
         mode_matmul(d, weighted_values, LAYER_T(l, 4), f_out, H, H);
         for (size_t i = 0; i < H; i++) token[i] = token[i] + f_out[i];

@@ -105,6 +105,9 @@ int orc_generate_capped(const orc_dims *d, const void *const *tensors,
 
 /* Thread count used by the parallel matvecs (Rayon's pool in the reference). */
 void orc_set_threads(int n);
+/* Test aid: buf (n_layers x embed_dim floats) receives each layer's attention
+ * output from the next orc_forward calls on; NULL stops it. */
+void orc_set_attn_dump(float *buf);
 /* 1: eight matrix rows per pass and attention heads in parallel (same bits,
  * faster; for the tests); 0 (default): the reference's loop order. */
 void orc_set_fast(int on);

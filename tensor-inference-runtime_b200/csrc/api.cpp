@@ -233,6 +233,7 @@ struct tir_state {
     std::vector<void*> allocs;
     float *x = nullptr, *x0 = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr;
     float *dump = nullptr, *kc = nullptr, *vc = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    uint8_t* qdump = nullptr;  // Mode::Quantize inputs of the last forward, [(2 L + 1)][H / 32] blocks
     float* attn_part = nullptr;
     uint32_t *attn_cnt = nullptr, *counters = nullptr, *error = nullptr;
     unsigned long long* argmax_part = nullptr;
@@ -745,6 +746,7 @@ tir_status tir_state_create(tir_model* m, int32_t max_ctx, tir_state** out) {
               alloc(H * 4, reinterpret_cast<void**>(&s->q)) && alloc(H * 4, reinterpret_cast<void**>(&s->attn)) &&
               alloc(F * 4, reinterpret_cast<void**>(&s->h)) && alloc(V * 4, reinterpret_cast<void**>(&s->logits)) &&
               alloc((L + 1) * H * 4, reinterpret_cast<void**>(&s->dump)) &&
+              alloc((2 * L + 1) * (H / 32) * 34, reinterpret_cast<void**>(&s->qdump)) &&
               alloc(cache_f * 4, reinterpret_cast<void**>(&s->kc)) && alloc(cache_f * 4, reinterpret_cast<void**>(&s->vc)) &&
               alloc(static_cast<size_t>(max_ctx) * 32 * 4, reinterpret_cast<void**>(&s->rope_cos)) &&
               alloc(static_cast<size_t>(max_ctx) * 32 * 4, reinterpret_cast<void**>(&s->rope_sin)) &&
@@ -831,6 +833,8 @@ static tir_status launch_steps(tir_state* s, int n_steps, int pos0, const float*
     p.rms_eps = 1e-5f;  // src/math.rs:144, whatever the file says
     p.x = s->x;
     p.dump = s->dump_on ? s->dump : nullptr;
+    p.qdump = s->dump_on && t.mode == 1 ? s->qdump : nullptr;
+    p.n_layers = static_cast<int32_t>(t.layers);
     p.rope_cos = s->rope_cos;
     p.rope_sin = s->rope_sin;
     p.attn_part = s->attn_part;
@@ -1074,6 +1078,20 @@ tir_status tir_debug_dump_layers(tir_state* s, float* out_host) {
                              s->stream),
              "dump readback");
     CUDA_TRY(cudaStreamSynchronize(s->stream), "dump readback");
+    return TIR_OK;
+}
+
+// The Q8_0 blocks Mode::Quantize made of the q|k|v, o and lm_head inputs in
+// the last forward (activated_q8, src/kernels.rs:8-31): [2 l] q|k|v of layer
+// l, [2 l + 1] o of layer l, [2 L] lm_head; needs the dump on and Mode 1.
+tir_status tir_debug_dump_qact(tir_state* s, uint8_t* out_host) {
+    clear_error();
+    if (!s || !out_host) return fail(TIR_ERR_INVALID_ARG, "null argument");
+    if (!s->dump_on || s->m->t.mode != 1) return fail(TIR_ERR_INVALID_ARG, "needs the dump on and Mode::Quantize");
+    CUDA_TRY(cudaSetDevice(s->m->device), "cudaSetDevice");
+    const size_t n = static_cast<size_t>(2 * s->m->t.layers + 1) * (s->m->t.embed_dim / 32) * 34;
+    CUDA_TRY(cudaMemcpyAsync(out_host, s->qdump, n, cudaMemcpyDeviceToHost, s->stream), "qact dump readback");
+    CUDA_TRY(cudaStreamSynchronize(s->stream), "qact dump readback");
     return TIR_OK;
 }
 

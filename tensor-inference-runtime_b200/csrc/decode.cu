@@ -630,6 +630,20 @@ __device__ __forceinline__ void stage_input_qact(const DecodeParams& p, Smem& s,
         *reinterpret_cast<uint4*>(&s.u.st.xd[1][b][4 * h]) = make_uint4(0u, 0u, 0u, 0u);
         *reinterpret_cast<uint4*>(&s.u.st.xd[2][b][4 * h]) = make_uint4(0u, 0u, 0u, 0u);
         if (h == 0) s.u.st.xsc[b] = __half2float(__float2half_rn(scale));
+        // the dump of the quantised input (Q8_0 blocks, as activated_q8 writes
+        // them), by one of the phase's CTAs: slot 2 l (q|k|v of layer l),
+        // 2 l + 1 (o of layer l), 2 L (lm_head)
+        if (p.qdump && s.tfirst[ph] == 0) {
+            const int slot = d.layer < 0 ? 2 * p.n_layers : 2 * d.layer + (d.epi == EPI_QKV ? 0 : 1);
+            uint8_t* blk = p.qdump + (static_cast<size_t>(slot) * (d.k / 32) + b) * 34;
+            if (h == 0) {
+                const unsigned short hs = __half_as_ushort(__float2half_rn(scale));
+                blk[0] = static_cast<uint8_t>(hs & 0xffu);
+                blk[1] = static_cast<uint8_t>(hs >> 8);
+            }
+#pragma unroll
+            for (int e = 0; e < 16; ++e) blk[2 + 16 * h + e] = static_cast<uint8_t>((w0[e / 4] >> (8 * (e % 4))) & 0xffu);
+        }
     }
     (void)inv;
     cbar();

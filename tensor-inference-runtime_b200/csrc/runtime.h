@@ -115,6 +115,8 @@ struct DecodeParams {
     // state buffers
     float* x;                  // residual stream [H]
     float* dump;               // optional [(layers+1)][H]
+    uint8_t* qdump;            // optional, Mode::Quantize: [(2 layers + 1)][H / 32] Q8_0 blocks of the quantised inputs
+    int32_t n_layers;
     const float* rope_cos;     // [max_ctx][32]
     const float* rope_sin;
     float* attn_part;          // [kv][max_splits][group][kAttnRec]

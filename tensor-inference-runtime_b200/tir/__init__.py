@@ -112,6 +112,7 @@ SIGNATURES = {
     "tir_state_enable_dump": (C.c_int, [_vp, C.c_int32]),
     "tir_state_dump": (C.c_int, [_vp, _f32p]),
     "tir_debug_dump_layers": (C.c_int, [_vp, _f32p]),
+    "tir_debug_dump_qact": (C.c_int, [_vp, _vp]),
     "tir_prefill": (C.c_int, [_vp, _vp, C.c_int32, C.c_int32, _vp]),
     "tir_state_enable_trace": (C.c_int, [_vp, C.c_int32]),
     "tir_state_trace_dims": (C.c_int, [_vp, _i32p, _i32p]),
@@ -523,6 +524,15 @@ class State:
 
     def enable_dump(self, on=True):
         check(lib().tir_state_enable_dump(self._h, 1 if on else 0))
+
+    def dump_qact(self):
+        """Mode::Quantize: [(2 L + 1), embed_dim / 32, 34] uint8 Q8_0 blocks of the
+        last forward's quantised inputs (q|k|v of layer l at 2 l, o at 2 l + 1,
+        lm_head at 2 L)."""
+        nb = self.embed_dim // 32
+        out = np.empty((2 * self.layers + 1, nb, 34), np.uint8)
+        check(lib().tir_debug_dump_qact(self._h, out.ctypes.data))
+        return out
 
     def enable_trace(self, step):
         check(lib().tir_state_enable_trace(self._h, int(step)))
