@@ -382,17 +382,41 @@ __global__ void gemm_repack_kernel(const uint8_t* __restrict__ blocks, int64_t n
 // magnitude and once for the split.
 constexpr int kPlaneThreads = 256;
 
-template <class F>
-__device__ __forceinline__ void planes_row(const F& val, bool live, int64_t t, int64_t k, int nt,
-                                           uint8_t* __restrict__ planes, float* __restrict__ inv) {
+// Each plane-writer thread owns columns [8 ch, 8 ch + 8) for its chunks
+// ch = tid + i * kPlaneThreads, i < plane_chunks(k), and keeps their values in
+// registers from the first read to the last write.
+constexpr int kPlaneMaxChunks = 3;  // k <= 3 x 8 x kPlaneThreads = 6144
+__device__ __forceinline__ int plane_chunks(int64_t k) {
+    const int64_t nch = k / 8;
+    const int64_t tid = threadIdx.x;
+    return tid < nch ? static_cast<int>((nch - 1 - tid) / kPlaneThreads + 1) : 0;
+}
+
+__device__ __forceinline__ void load8(const float* p, float* v) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void store8(float* p, const float* v) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// The planes of token row t from the thread's register values v (chunk i at
+// v[8 i]): the row's largest magnitude m (a CTA reduction) sets 2^kx with
+// m * 2^kx in [2^9, 2^10), then each value * 2^kx is split into f16 hi + lo
+// and stored into the 128B-swizzled hi and lo planes of its (token tile,
+// K step); inv[t] = 2^-kx.  A row that is not live gets zero planes.
+__device__ __forceinline__ void planes_store(const float* v, int nc, bool live, int64_t t, int64_t k, int nt,
+                                             uint8_t* __restrict__ planes, float* __restrict__ inv) {
     __shared__ float red[kPlaneThreads / 32];
     const int tid = threadIdx.x;
-    const int64_t nch = k / 8;
     float mx = 0.f;
     if (live)
-        for (int64_t ch = tid; ch < nch; ch += kPlaneThreads)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(val(ch * 8 + j)));
+        for (int i = 0; i < kPlaneMaxChunks * 8; ++i)
+            if (i < nc * 8) mx = fmaxf(mx, fabsf(v[i]));
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((tid & 31) == 0) red[tid >> 5] = mx;
@@ -410,16 +434,18 @@ __device__ __forceinline__ void planes_row(const F& val, bool live, int64_t t, i
     const int64_t plane = static_cast<int64_t>(nt) * kGKS * 2;
     const int64_t nks = k / kGKS, ttile = t / nt;
     const int tr = static_cast<int>(t % nt);
-    for (int64_t ch = tid; ch < nch; ch += kPlaneThreads) {
-        const int64_t c0 = ch * 8, ks = c0 / kGKS;
+#pragma unroll
+    for (int i = 0; i < kPlaneMaxChunks; ++i) {
+        if (i >= nc) break;
+        const int64_t c0 = (static_cast<int64_t>(tid) + static_cast<int64_t>(i) * kPlaneThreads) * 8, ks = c0 / kGKS;
         const int cc = static_cast<int>(c0 % kGKS);
         uint4 hv, lv;
         uint32_t* hp = &hv.x;
         uint32_t* lp = &lv.x;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float v0 = live ? val(c0 + 2 * j) * sx : 0.f;
-            const float v1 = live ? val(c0 + 2 * j + 1) * sx : 0.f;
+            const float v0 = live ? v[8 * i + 2 * j] * sx : 0.f;
+            const float v1 = live ? v[8 * i + 2 * j + 1] * sx : 0.f;
             const __half2 hi = __floats2half2_rn(v0, v1);
             const float2 hf = __half22float2(hi);
             const __half2 lo = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
@@ -441,19 +467,24 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_x_planes_kernel(const floa
     griddep_launch_dependents();
     griddep_wait();
     const int64_t t = blockIdx.x;
-    const float* row = x + t * k;
-    planes_row([&](int64_t c) { return row[c]; }, t < tokens, t, k, nt, planes, inv);
+    const bool live = t < tokens;
+    const int nc = plane_chunks(k);
+    float v[kPlaneMaxChunks * 8];
+#pragma unroll
+    for (int i = 0; i < kPlaneMaxChunks; ++i)
+        if (i < nc && live) load8(x + t * k + (threadIdx.x + static_cast<int64_t>(i) * kPlaneThreads) * 8, v + 8 * i);
+    planes_store(v, nc, live, t, k, nt, planes, inv);
 }
 
 // Planes of rmsnorm(h) * w (src/math.rs:141-150, the division as a
 // multiplication by the correctly rounded reciprocal), h = row
 // rows ? rows[t] : t of X -- after X += Y on that row when Y is given (the
 // residual add of src/forward.rs, fused here so the matmul before it only
-// stores), Y the sum of y_parts partial tiles y_part floats apart.  Gathered
-// row indices must be distinct (each row's tile 0 takes its sum in place);
-// rows[t] < 0 marks an unused slot (zero planes).
+// stores; X keeps the sum), Y the sum of y_parts partial tiles y_part floats
+// apart, added in partial order.  rows[t] < 0 marks an unused slot (zero
+// planes).
 __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* __restrict__ X,
-                                                                         float* __restrict__ Y, int y_parts,
+                                                                         const float* __restrict__ Y, int y_parts,
                                                                          int64_t y_part,
                                                                          const int32_t* __restrict__ rows,
                                                                          int64_t tokens, int64_t k,
@@ -467,31 +498,51 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_norm_planes_kernel(float* 
     // a gathered row index < 0 (an idle sequence) is not live: zero planes
     const int64_t xg = t < tokens ? (rows ? static_cast<int64_t>(rows[t]) : t) : -1;
     const bool live = xg >= 0;
-    const int64_t xr = live ? xg : 0;
-    float* x = X + xr * k;
-    if (Y) {
-        float* y = Y + xr * k;  // partial tile 0 takes the sum
-        sum_parts_inplace(y, live ? y_parts : 1, y_part, static_cast<int>(k));
-        if (live)
-            for (int64_t c = threadIdx.x; c < k; c += kPlaneThreads) x[c] = __fadd_rn(x[c], y[c]);
-        __syncthreads();
-    }
+    const int nc = plane_chunks(k);
+    float v[kPlaneMaxChunks * 8];
     float ss = 0.f;
-    if (live)
-        for (int64_t c = threadIdx.x; c < k; c += kPlaneThreads) ss = fmaf(x[c], x[c], ss);
+#pragma unroll
+    for (int i = 0; i < kPlaneMaxChunks; ++i) {
+        if (i >= nc || !live) continue;
+        const int64_t c0 = (threadIdx.x + static_cast<int64_t>(i) * kPlaneThreads) * 8;
+        float* x = X + xg * k + c0;
+        load8(x, v + 8 * i);
+        if (Y) {
+            float y[8], yj[8];
+            load8(Y + xg * k + c0, y);
+            for (int j = 1; j < y_parts; ++j) {
+                load8(Y + j * y_part + xg * k + c0, yj);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) y[u] = __fadd_rn(y[u], yj[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[8 * i + u] = __fadd_rn(v[8 * i + u], y[u]);
+            store8(x, v + 8 * i);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) ss = fmaf(v[8 * i + u], v[8 * i + u], ss);
+    }
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
     __syncthreads();
     float total = 0.f;
     for (int i = 0; i < kPlaneThreads / 32; ++i) total += part[i];
     const float r = __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(k)), eps)));
-    planes_row([&](int64_t c) { return __fmul_rn(__fmul_rn(x[c], w[c]), r); }, live, t, k, nt, planes, inv);
+#pragma unroll
+    for (int i = 0; i < kPlaneMaxChunks; ++i) {
+        if (i >= nc || !live) continue;
+        float wv[8];
+        load8(w + (threadIdx.x + static_cast<int64_t>(i) * kPlaneThreads) * 8, wv);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[8 * i + u] = __fmul_rn(__fmul_rn(v[8 * i + u], wv[u]), r);
+    }
+    planes_store(v, nc, live, t, k, nt, planes, inv);
 }
 
 // Planes of h[t][j] = silu(gate) * up from interleaved (gate_j, up_j) columns
 // of GU [tokens][2 f] (src/math.rs:171-175), GU the sum of `parts` partial
-// tiles `part` floats apart.
-__global__ void __launch_bounds__(kPlaneThreads) gemm_silu_planes_kernel(float* __restrict__ gu, int parts,
+// tiles `part` floats apart, added in partial order.
+__global__ void __launch_bounds__(kPlaneThreads) gemm_silu_planes_kernel(const float* __restrict__ gu, int parts,
                                                                          int64_t part, int64_t tokens, int64_t f,
                                                                          int nt,
                                                                          uint8_t* __restrict__ planes,
@@ -499,14 +550,27 @@ __global__ void __launch_bounds__(kPlaneThreads) gemm_silu_planes_kernel(float* 
     griddep_launch_dependents();
     griddep_wait();
     const int64_t t = blockIdx.x;
-    float* row = gu + t * 2 * f;  // partial tile 0 takes the sum
-    sum_parts_inplace(row, t < tokens ? parts : 1, part, static_cast<int>(2 * f));
-    planes_row(
-        [&](int64_t j) {
-            const float2 p = *reinterpret_cast<const float2*>(row + 2 * j);
-            return __fmul_rn(__fdiv_rn(p.x, __fadd_rn(1.0f, expf(-p.x))), p.y);
-        },
-        t < tokens, t, f, nt, planes, inv);
+    const bool live = t < tokens;
+    const int nc = plane_chunks(f);
+    float v[kPlaneMaxChunks * 8];
+#pragma unroll
+    for (int i = 0; i < kPlaneMaxChunks; ++i) {
+        if (i >= nc || !live) continue;
+        const float* row = gu + t * 2 * f + (threadIdx.x + static_cast<int64_t>(i) * kPlaneThreads) * 16;
+        float a[16], b[16];
+        load8(row, a);
+        load8(row + 8, a + 8);
+        for (int j = 1; j < parts; ++j) {
+            load8(row + j * part, b);
+            load8(row + j * part + 8, b + 8);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) a[u] = __fadd_rn(a[u], b[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            v[8 * i + u] = __fmul_rn(__fdiv_rn(a[2 * u], __fadd_rn(1.0f, expf(-a[2 * u]))), a[2 * u + 1]);
+    }
+    planes_store(v, nc, live, t, f, nt, planes, inv);
 }
 
 }  // namespace

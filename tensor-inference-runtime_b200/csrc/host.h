@@ -150,15 +150,16 @@ int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out
 int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream,
                          bool pdl = false);
 // Planes of rmsnorm(X[r]) * w, r = rows ? rows[t] : t for t < tokens, after
-// X[r] += Y[r] when Y is not null, Y the sum of y_parts partial tiles y_part
-// floats apart (summed into tile 0).  Gathered rows must be distinct; a
-// negative rows[t] gives zero planes for t.
+// X[r] += Y[r] when Y is not null (X keeps the sum), Y the sum of y_parts
+// partial tiles y_part floats apart, added in partial order (Y is left as it
+// is).  Gathered rows must be distinct; a negative rows[t] gives zero planes
+// for t.
 int launch_gemm_norm_planes(float* X, float* Y, int y_parts, int64_t y_part, const int32_t* rows, int64_t tokens,
                             int64_t k, const float* w, float eps, uint8_t* planes, float* inv, void* stream,
                             bool pdl = false);
 // Planes of silu(gate) * up from interleaved (gate, up) columns of gu
-// [tokens][2 f], the sum of `parts` partial tiles `part` floats apart
-// (summed into tile 0).
+// [tokens][2 f], the sum of `parts` partial tiles `part` floats apart, added
+// in partial order (gu is left as it is).
 int launch_gemm_silu_planes(float* gu, int parts, int64_t part, int64_t tokens, int64_t f, uint8_t* planes,
                             float* inv, void* stream, bool pdl = false);
 // Shared-memory opt-in of the matmul kernels on the current device (0 or a cudaError_t).
