@@ -365,15 +365,28 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
             m[h] = m_new;
             p[h] = pj;
         }
+        // value rows eight keys at a time: the loads of the eight are in
+        // flight together, then folded in key order
         const int nc = min(32, n - c0);
-        for (int jj = 0; jj < nc; ++jj) {
-            const float* vr = vc + kv_slot(pg, s, c0 + jj, kvd) + head;
-            const float v0 = vr[lane], v1 = vr[lane + 32];
+        for (int j0 = 0; j0 < nc; j0 += 8) {
+            float v0[8], v1[8];
 #pragma unroll
-            for (int h = 0; h < G; ++h) {
-                const float pt = __shfl_sync(0xffffffffu, p[h], jj);
-                o0[h] = fmaf(pt, v0, o0[h]);
-                o1[h] = fmaf(pt, v1, o1[h]);
+            for (int u = 0; u < 8; ++u) {
+                const int jj = min(j0 + u, nc - 1);
+                const float* vr = vc + kv_slot(pg, s, c0 + jj, kvd) + head;
+                v0[u] = vr[lane];
+                v1[u] = vr[lane + 32];
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (j0 + u < nc) {
+#pragma unroll
+                    for (int h = 0; h < G; ++h) {
+                        const float pt = __shfl_sync(0xffffffffu, p[h], j0 + u);
+                        o0[h] = fmaf(pt, v0[u], o0[h]);
+                        o1[h] = fmaf(pt, v1[u], o1[h]);
+                    }
+                }
             }
         }
     }
