@@ -41,7 +41,8 @@ namespace {
 
 constexpr int kGM = 128;    // weight rows per tile (UMMA M)
 constexpr int kGKS = 64;    // K per stage: one 128-byte f16 row
-constexpr int kGThreads = 192;
+constexpr int kGConvWarps = 8;  // weight converters, then the epilogue (two warps per TMEM lane quarter)
+constexpr int kGThreads = 64 + 32 * kGConvWarps;
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
 constexpr int kGPlaneA = kGM * kGKS * 2;            // one f16 weight plane of a stage (16 KB)
 constexpr uint32_t kGErrTimeout = 25;
@@ -49,6 +50,13 @@ constexpr int kGMaxSplits = 16;  // split-K CTAs per tile
 
 template <int NT>
 struct GemmCfg {
+    // Small token tiles issue a_hi x [x_hi | x_lo] as one MMA of N = 2 NT
+    // (the two activation planes are adjacent rows of one K-major operand),
+    // accumulating into TMEM columns [0, 2 NT), and a_lo x x_hi into [0, NT);
+    // the epilogue adds column c and c + NT.  Large tiles issue the three
+    // passes separately (N is at most 256).
+    static constexpr bool kMergeLo = 2 * NT <= 256;
+    static constexpr int kTmemCols = kMergeLo ? 2 * NT : NT;
     // TMA ring (raw weight block + activation planes of a K step): deep for
     // small token tiles, whose steps are short, so that HBM latency is covered.
     static constexpr int kRaw = NT >= 256 ? 2 : 6;
@@ -160,10 +168,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         for (int i = 0; i < kRaw; ++i) {
             mbar_init(&s.full_w[i], 1);
             mbar_init(&s.full_x[i], 1);
-            mbar_init(&s.empty_raw[i], 4 + 1);  // the 4 converter warps + the MMAs' commit
+            mbar_init(&s.empty_raw[i], kGConvWarps + 1);  // the converter warps + the MMAs' commit
         }
         for (int i = 0; i < kConv; ++i) {
-            mbar_init(&s.full_a[i], 4);
+            mbar_init(&s.full_a[i], kGConvWarps);
             mbar_init(&s.empty_a[i], 1);
         }
         mbar_init(&s.acc, 1);
@@ -172,7 +180,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem_base)),
-                     "r"(static_cast<uint32_t>(NT)));
+                     "r"(static_cast<uint32_t>(GemmCfg<NT>::kTmemCols)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -221,6 +229,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         // ---- MMA issue (one thread)
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(NT >> 3) << 17) | (static_cast<uint32_t>(kGM >> 4) << 24);
+            const uint32_t idesc2 =
+                (1u << 4) | (static_cast<uint32_t>((2 * NT) >> 3) << 17) | (static_cast<uint32_t>(kGM >> 4) << 24);
             for (int i = 0; i < nks; ++i) {
                 const int st = i % kRaw, sa = i % kConv;
                 if (!gwait(p, &s.full_x[st], (i / kRaw) & 1) || !gwait(p, &s.full_a[sa], (i / kConv) & 1)) {
@@ -233,8 +243,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
 #pragma unroll
                 for (int kk = 0; kk < kGKS / 16; ++kk) {
                     const uint32_t o = kk * 32;
-                    umma_f16(tmem, umma_desc(a_hi + o), umma_desc(x_hi + o), idesc, (i > 0 || kk > 0) ? 1u : 0u);
-                    umma_f16(tmem, umma_desc(a_hi + o), umma_desc(x_lo + o), idesc, 1u);
+                    if constexpr (GemmCfg<NT>::kMergeLo) {
+                        umma_f16(tmem, umma_desc(a_hi + o), umma_desc(x_hi + o), idesc2, (i > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        umma_f16(tmem, umma_desc(a_hi + o), umma_desc(x_hi + o), idesc, (i > 0 || kk > 0) ? 1u : 0u);
+                        umma_f16(tmem, umma_desc(a_hi + o), umma_desc(x_lo + o), idesc, 1u);
+                    }
                     umma_f16(tmem, umma_desc(a_lo + o), umma_desc(x_hi + o), idesc, 1u);
                 }
                 // the weight planes and the activation planes are free once these MMAs completed
@@ -244,17 +258,18 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
             umma_commit(&s.acc);
         }
     } else {
-        // ---- converters: thread r expands weight row r of each step.  The raw
+        // ---- converters: threads r and r + 128 expand weight row r of each
+        // step, columns 0..31 and 32..63.  The raw
         // block holds q + 128 as bytes and f16 scales already multiplied by
         // the row's 2^kw, so a = q * s' (at most 19 significant bits, below
         // 2^15) splits in packed f16 arithmetic: hi = RN(q * s'), and
         // lo = q * s' - hi, exact in one fused multiply-add (at most 8
         // significant bits, all at or above the last bit of s').  Bytes become
         // f16 by the magic-number route: 0x64 << 8 | b is the f16 1024 + b.
-        const int r = tid - 64;
-        uint32_t offs[8];
+        const int r = (tid - 64) & (kGM - 1), hc = (tid - 64) >> 7;  // row, column half
+        uint32_t offs[4];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) offs[ch] = sw128_offset(r, ch * 8);
+        for (int ch = 0; ch < 4; ++ch) offs[ch] = sw128_offset(r, (4 * hc + ch) * 8);
         const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
         bool ok = true;
         for (int i = 0; i < nks && ok; ++i) {
@@ -262,15 +277,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
             ok = gwait(p, &s.full_w[st], (i / kRaw) & 1);
             if (ok && i >= kConv) ok = gwait(p, &s.empty_a[sa], ((i / kConv) - 1) & 1);
             if (ok) {
-                const uint8_t* wq = s.w[st] + r * kGKS;
+                const uint8_t* wq = s.w[st] + r * kGKS + 32 * hc;
                 const __half2 sc2 = reinterpret_cast<const __half2*>(s.w[st] + kGM * kGKS)[r];
-                const __half2 s0 = __low2half2(sc2), s1 = __high2half2(sc2);
+                const __half2 sc = hc ? __high2half2(sc2) : __low2half2(sc2);
                 uint8_t* ahi = s.a[sa];
                 uint8_t* alo = s.a[sa] + kGPlaneA;
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) {  // 8 columns per 16-byte chunk
+                for (int ch = 0; ch < 4; ++ch) {  // 8 columns per 16-byte chunk
                     const uint2 qv = *reinterpret_cast<const uint2*>(wq + ch * 8);
-                    const __half2 sc = ch < 4 ? s0 : s1;
                     uint4 hv, lv;
                     uint32_t* hp = &hv.x;
                     uint32_t* lp = &lv.x;
@@ -295,11 +309,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                 mbar_arrive(&s.empty_raw[st]);
             }
         }
-        // ---- epilogue: TMEM lane quarter (warp % 4) holds weight rows 32 q .. 32 q + 31;
-        // it reads 2^-kx per token and may add into y: after earlier work
+        // ---- epilogue: TMEM lane quarter (warp % 4) holds weight rows 32 q .. 32 q + 31,
+        // read by two warps, each half of the tile's tokens; it reads 2^-kx per
+        // token and may add into y: after earlier work
         griddep_wait();
-        for (int i = tid - 64; i < NT; i += 128) s.inv_x[i] = p.x_inv[tt * NT + i];
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+        for (int i = tid - 64; i < NT; i += 32 * kGConvWarps) s.inv_x[i] = p.x_inv[tt * NT + i];
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kGConvWarps) : "memory");  // the epilogue warps
         const bool acc_ok = __all_sync(0xffffffffu, ok && gwait(p, &s.acc, 0));
         tc_fence_after();
         const int q = warp & 3;
@@ -311,9 +326,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         // `split` of y ([splits][tokens][y_ld]); the reader adds them up
         float* y = p.y + static_cast<size_t>(split) * p.tokens * p.y_ld;
         if (acc_ok) {  // warp-uniform: the TMEM loads are warp-collective
-            for (int c0 = 0; c0 < NT; c0 += 16) {
+            const int half = (warp - 2) >> 2;
+            for (int c0 = half * (NT / 2); c0 < (half + 1) * (NT / 2); c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
+                if constexpr (GemmCfg<NT>::kMergeLo) {  // + a_hi x x_lo from columns NT..2 NT
+                    uint32_t w[16];
+                    tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + NT + c0, w);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int t = tt * NT + c0 + j;
@@ -326,7 +348,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     tc_fence_before();
     __syncthreads();
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                                "r"(static_cast<uint32_t>(NT)));
+                                "r"(static_cast<uint32_t>(GemmCfg<NT>::kTmemCols)));
 }
 
 // ---- layouts -----------------------------------------------------------------
