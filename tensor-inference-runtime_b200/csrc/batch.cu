@@ -17,6 +17,7 @@
 #include "host.h"
 #include "launch.cuh"
 #include "parts.cuh"
+#include "planes.cuh"
 #include "ptx.cuh"
 #include "runtime.h"
 
@@ -263,18 +264,25 @@ __global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const flo
 // (queries in shared memory), the warp folds the chunk into a running (max,
 // sum, output) per head with lanes over output dimensions, and the warps'
 // states merge at the end.  Scale 1/sqrt(64), softmax with the running-max
-// shift.
+// shift.  The last of a sequence's kv-head CTAs to finish (head_done[s]
+// counts them and is reset by that CTA) turns the sequence's output row into
+// the activation planes of the o projection (planes.cuh), which the plane
+// writer would otherwise do as a kernel of its own.
 constexpr int kAttnWarps = 8;
+static_assert(kAttnWarps * 32 == kPlaneThreads, "the decode attention CTA writes planes with all its threads");
 constexpr int kMaxParts = 16;  // split-K partial tiles a reader sums
 
 template <int G>  // query heads per kv head, rounded up (heads >= group are computed on zeros, not stored)
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const float* __restrict__ qkv, int parts,
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const float* __restrict__ qkv, int parts,
                                                                       int64_t part, int64_t ld, Pages pg, int H,
                                                                       int kvd, int group, const float* __restrict__ rc,
                                                                       const float* __restrict__ rs,
                                                                       float* __restrict__ kc,
                                                                       float* __restrict__ vc,
-                                                                      float* __restrict__ out) {
+                                                                      float* __restrict__ out,
+                                                                      uint32_t* __restrict__ head_done, int nt,
+                                                                      uint8_t* __restrict__ planes,
+                                                                      float* __restrict__ inv) {
     griddep_launch_dependents();
     griddep_wait();
     __shared__ __align__(16) float qs[G][kHeadDim];
@@ -414,6 +422,24 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(const floa
         }
         out[r * H + (g * group + h) * kHeadDim + d] = O / L;
     }
+    __shared__ bool last;
+    __syncthreads();  // the CTA's part of the row is written
+    if (threadIdx.x == 0) {
+        __threadfence();  // ... and visible before the count
+        last = atomicAdd(&head_done[s], 1u) == gridDim.y - 1;
+        if (last) {
+            head_done[s] = 0;  // ready for the next launch
+            __threadfence();   // the other heads' parts visible to this CTA
+        }
+    }
+    __syncthreads();
+    if (!last) return;
+    const int nc = plane_chunks(H);
+    float v[kPlaneMaxChunks * 8];
+#pragma unroll
+    for (int i = 0; i < kPlaneMaxChunks; ++i)
+        if (i < nc) load8_cg(out + r * H + (threadIdx.x + i * kPlaneThreads) * 8, v + 8 * i);
+    planes_store(v, nc, true, r, H, nt, planes, inv);
 }
 
 // Greedy sample per row (src/tokenizer.rs:152-167: total order, ties -> last)
@@ -515,6 +541,7 @@ struct tir_batch {
     float* logits = nullptr;  // [B][V] summed lm_head rows (allocated on first tir_batch_logits)
     int lm_parts = 0;         // partial tiles of the last forward's lm_head output (0: no forward yet)
     uint32_t *err = nullptr, *h_err = nullptr;
+    uint32_t* head_done = nullptr;  // [B] kv-head CTAs of the decode attention done (zero between launches)
     // Sequences and pages.  seq_len lives on the device (kernels read and
     // advance it, so graph replays stay valid); h_len mirrors it.
     int32_t* seq_len = nullptr;
@@ -622,7 +649,7 @@ void attn_decode(tir_batch* b, const Pages& pg, int64_t rows, int parts, int gro
     const int64_t part = rows * ldq;
 #define TIR_ATTN(GM)                                                                                                   \
     launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, parts, part, ldq, pg, H, KVD,    \
-                  group, b->rcos, b->rsin, kc, vc, b->ATT)
+                  group, b->rcos, b->rsin, kc, vc, b->ATT, b->head_done, gemm_token_tile(rows), b->planes, b->inv)
     if (group <= 1)
         TIR_ATTN(1);
     else if (group <= 2)
@@ -675,7 +702,7 @@ tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
         float* kc = b->kc + l * layer_cache;
         float* vc = b->vc + l * layer_cache;
         if (max_cnt <= 1) {
-            attn_decode(b, pg, T, parts, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);
+            attn_decode(b, pg, T, parts, group, static_cast<int>(t.k_v_heads), H, KVD, ldq, kc, vc);  // + the planes
         } else {
             launch_kernel(rope_append_kernel, dim3(static_cast<unsigned>(T)), dim3(256), 0, st, true, b->QKV, parts,
                           T * ldq, ldq, pg, H, KVD, b->rcos, b->rsin, kc, vc);
@@ -683,8 +710,8 @@ tir_status forward(tir_batch* b, const int32_t* meta, int64_t T, int max_cnt) {
                           dim3(b->B, static_cast<unsigned>(t.k_v_heads * ((group + kPHeads - 1) / kPHeads)),
                                (max_cnt + kQBlock - 1) / kQBlock),
                           dim3(kPHeads * 32), 0, st, true, b->QKV, ldq, pg, H, KVD, group, kc, vc, b->ATT);
+            if ((rc = planes_rc(launch_gemm_x_planes(b->ATT, T, H, b->planes, b->inv, st, true))) != TIR_OK) return rc;
         }
-        if ((rc = planes_rc(launch_gemm_x_planes(b->ATT, T, H, b->planes, b->inv, st, true))) != TIR_OK) return rc;
         if ((rc = mm(b, T, b->o[l], b->Y, &y_parts)) != TIR_OK) return rc;
         if ((rc = planes_rc(launch_gemm_norm_planes(b->X, b->Y, y_parts, T * H, nullptr, T, H, m->ffn_norm[l], 1e-5f,
                                                     b->planes, b->inv, st, true))) != TIR_OK)
@@ -914,7 +941,8 @@ tir_status tir_batch_create_paged(tir_model* m, int32_t n_seqs, int32_t max_ctx,
               balloc(b, static_cast<size_t>(gemm_x_plane_bytes(T, kmax)), &b->planes) &&
               balloc(b, static_cast<size_t>(gemm_tokens_padded(T)) * 4, &b->inv) && balloc(b, T * 4, &b->ids) &&
               balloc(b, static_cast<size_t>(n_seqs) * 4, &b->rows) &&
-              balloc(b, static_cast<size_t>(n_seqs) * 4, &b->next) && balloc(b, 16, &b->err);
+              balloc(b, static_cast<size_t>(n_seqs) * 4, &b->next) && balloc(b, 16, &b->err) &&
+              balloc(b, static_cast<size_t>(n_seqs) * 4, &b->head_done);
     if (!ok || host_malloc_pinned(&b->h_next, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
         host_malloc_pinned(&b->h_err, 16) != cudaSuccess ||
         host_malloc_pinned(&b->h_table, static_cast<size_t>(n_seqs) * b->max_pages * 4) != cudaSuccess ||
@@ -936,6 +964,7 @@ tir_status tir_batch_create_paged(tir_model* m, int32_t n_seqs, int32_t max_ctx,
         cudaMemcpy(b->uni, uni.data(), uni.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemset(b->table, 0, static_cast<size_t>(n_seqs) * b->max_pages * 4) != cudaSuccess ||
         cudaMemset(b->err, 0, 16) != cudaSuccess || cudaMemset(b->seq_len, 0, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
+        cudaMemset(b->head_done, 0, static_cast<size_t>(n_seqs) * 4) != cudaSuccess ||
         gemm_configure() != 0) {
         delete b;
         return fail(TIR_ERR_CUDA, "batch initialisation failed");

@@ -32,6 +32,7 @@
 #include "host.h"
 #include "launch.cuh"
 #include "parts.cuh"
+#include "planes.cuh"
 #include "ptx.cuh"
 #include "runtime.h"
 
@@ -40,7 +41,6 @@ namespace tir {
 namespace {
 
 constexpr int kGM = 128;    // weight rows per tile (UMMA M)
-constexpr int kGKS = 64;    // K per stage: one 128-byte f16 row
 constexpr int kGConvWarps = 8;  // weight converters, then the epilogue (two warps per TMEM lane quarter)
 constexpr int kGThreads = 64 + 32 * kGConvWarps;
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
@@ -91,11 +91,6 @@ struct GemmParams {
     unsigned long long timeout_ns;
 };
 
-// Byte offset of f16 element (row r, column c < 64) in a 128B-swizzled K-major
-// plane: 8-row atoms of 1 KB, 16-byte chunk index XORed with r % 8.
-__host__ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
-    return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 3) ^ (r & 7)) & 7) << 4) + (c & 7) * 2);
-}
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
     // start address, LBO 16 B (unused with swizzle), SBO 1 KB, version 1, SWIZZLE_128B
@@ -402,85 +397,6 @@ __global__ void gemm_repack_kernel(const uint8_t* __restrict__ blocks, int64_t n
 // per token row (rows t >= tokens of the last tile are written as zeros);
 // val(c) gives column c of the row, evaluated once for the row's largest
 // magnitude and once for the split.
-constexpr int kPlaneThreads = 256;
-
-// Each plane-writer thread owns columns [8 ch, 8 ch + 8) for its chunks
-// ch = tid + i * kPlaneThreads, i < plane_chunks(k), and keeps their values in
-// registers from the first read to the last write.
-constexpr int kPlaneMaxChunks = 3;  // k <= 3 x 8 x kPlaneThreads = 6144
-__device__ __forceinline__ int plane_chunks(int64_t k) {
-    const int64_t nch = k / 8;
-    const int64_t tid = threadIdx.x;
-    return tid < nch ? static_cast<int>((nch - 1 - tid) / kPlaneThreads + 1) : 0;
-}
-
-__device__ __forceinline__ void load8(const float* p, float* v) {
-    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
-__device__ __forceinline__ void store8(float* p, const float* v) {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-}
-
-// The planes of token row t from the thread's register values v (chunk i at
-// v[8 i]): the row's largest magnitude m (a CTA reduction) sets 2^kx with
-// m * 2^kx in [2^9, 2^10), then each value * 2^kx is split into f16 hi + lo
-// and stored into the 128B-swizzled hi and lo planes of its (token tile,
-// K step); inv[t] = 2^-kx.  A row that is not live gets zero planes.
-__device__ __forceinline__ void planes_store(const float* v, int nc, bool live, int64_t t, int64_t k, int nt,
-                                             uint8_t* __restrict__ planes, float* __restrict__ inv) {
-    __shared__ float red[kPlaneThreads / 32];
-    const int tid = threadIdx.x;
-    float mx = 0.f;
-    if (live)
-#pragma unroll
-        for (int i = 0; i < kPlaneMaxChunks * 8; ++i)
-            if (i < nc * 8) mx = fmaxf(mx, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((tid & 31) == 0) red[tid >> 5] = mx;
-    __syncthreads();
-    mx = red[0];
-#pragma unroll
-    for (int i = 1; i < kPlaneThreads / 32; ++i) mx = fmaxf(mx, red[i]);
-    int e = 0;
-    float sx = 0.f, isx = 0.f;
-    if (mx > 0.f && mx < 3.0e38f) {
-        frexpf(mx, &e);  // 2^(e-1) <= mx < 2^e
-        sx = ldexpf(1.0f, 10 - e);
-        isx = ldexpf(1.0f, e - 10);
-    }
-    const int64_t plane = static_cast<int64_t>(nt) * kGKS * 2;
-    const int64_t nks = k / kGKS, ttile = t / nt;
-    const int tr = static_cast<int>(t % nt);
-#pragma unroll
-    for (int i = 0; i < kPlaneMaxChunks; ++i) {
-        if (i >= nc) break;
-        const int64_t c0 = (static_cast<int64_t>(tid) + static_cast<int64_t>(i) * kPlaneThreads) * 8, ks = c0 / kGKS;
-        const int cc = static_cast<int>(c0 % kGKS);
-        uint4 hv, lv;
-        uint32_t* hp = &hv.x;
-        uint32_t* lp = &lv.x;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float v0 = live ? v[8 * i + 2 * j] * sx : 0.f;
-            const float v1 = live ? v[8 * i + 2 * j + 1] * sx : 0.f;
-            const __half2 hi = __floats2half2_rn(v0, v1);
-            const float2 hf = __half22float2(hi);
-            const __half2 lo = __floats2half2_rn(v0 - hf.x, v1 - hf.y);
-            hp[j] = *reinterpret_cast<const uint32_t*>(&hi);
-            lp[j] = *reinterpret_cast<const uint32_t*>(&lo);
-        }
-        uint8_t* base = planes + (ttile * nks + ks) * (2 * plane);
-        const uint32_t off = sw128_offset(tr, cc);
-        *reinterpret_cast<uint4*>(base + off) = hv;
-        *reinterpret_cast<uint4*>(base + plane + off) = lv;
-    }
-    if (tid == 0) inv[t] = isx;
-}
 
 // Planes of X [tokens][k] as given.
 __global__ void __launch_bounds__(kPlaneThreads) gemm_x_planes_kernel(const float* __restrict__ x, int64_t tokens,

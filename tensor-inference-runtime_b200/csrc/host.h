@@ -145,6 +145,7 @@ int64_t gemm_q8_weight_bytes(int64_t n, int64_t k);
 int64_t gemm_q8_rows_padded(int64_t n);
 int64_t gemm_x_plane_bytes(int64_t tokens, int64_t k);
 int64_t gemm_tokens_padded(int64_t tokens);
+int gemm_token_tile(int64_t tokens);  // token rows per matmul tile (64 or 256)
 int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out, float* pow2, void* stream);
 // pdl: launched with a programmatic dependency on the stream's previous work.
 int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream,
