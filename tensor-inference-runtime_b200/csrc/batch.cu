@@ -255,20 +255,31 @@ __global__ void __launch_bounds__(kPHeads * 32, 1) attn_prefill_kernel(const flo
 }
 
 // One new token per sequence (decode), src/forward.rs:79-174: CTA per
-// (sequence, kv head).  First the CTA finishes the q|k|v projection for its
-// kv head (the sum of the matmul's `parts` partial tiles), applies RoPE to its
-// query heads and key (src/math.rs:196-228) and appends key and value to the
-// cache (src/forward.rs:83-84).  Then kAttnWarps warps split the key
-// positions in chunks of 32 (warp w takes chunks w, w + kAttnWarps, ...):
-// lane j scores key j of its chunk against every query head of the group
-// (queries in shared memory), the warp folds the chunk into a running (max,
-// sum, output) per head with lanes over output dimensions, and the warps'
-// states merge at the end.  Scale 1/sqrt(64), softmax with the running-max
-// shift.  The last of a sequence's kv-head CTAs to finish (head_done[s]
-// counts them and is reset by that CTA) turns the sequence's output row into
-// the activation planes of the o projection (planes.cuh), which the plane
-// writer would otherwise do as a kernel of its own.
+// (sequence, kv head).  The CTA finishes the q|k|v projection for its kv head
+// (the sum of the matmul's `parts` partial tiles), applies RoPE to its query
+// heads and key (src/math.rs:196-228) and appends key and value to the cache
+// (src/forward.rs:83-84).  Key and value rows are read from shared memory, in
+// windows of kAttnWin positions staged with cp.async.  The first window is
+// requested before the wait on the q|k|v matmul: the positions before the
+// new one were written by earlier forwards, and every forward starts after a
+// stream operation that is not a programmatic launch (the decode graph's
+// launch, or the copy of the step layout), so those forwards are complete;
+// the page table and the step layout do not change during a forward.  Warp w
+// takes the 32-key chunks w, w + kAttnWarps, ... of a window: lane j scores
+// key j against every query head of the group (queries in shared memory),
+// the chunk's probabilities go to shared memory, and the warp folds the
+// chunk into a running (max, sum, output) per head with lanes over output
+// dimensions; the warps' states merge at the end.  Scale 1/sqrt(64), softmax
+// with the running-max shift.  The last of a sequence's kv-head CTAs to
+// finish (head_done[s] counts them and is reset by that CTA) turns the
+// sequence's output row into the activation planes of the o projection
+// (planes.cuh), which the plane writer would otherwise do as a kernel of its
+// own.
 constexpr int kAttnWarps = 8;
+constexpr int kAttnWin = 176;         // positions per staged window (two CTAs per SM)
+constexpr int kKVPad = kHeadDim + 4;  // floats per staged row: 16-byte reads of 8 rows hit distinct banks
+constexpr int kAttnPid = 256;         // page ids staged in shared memory (later pages: read from the table)
+constexpr size_t kAttnDynSmem = 2u * kAttnWin * kKVPad * sizeof(float);  // [K | V][row][kKVPad]
 static_assert(kAttnWarps * 32 == kPlaneThreads, "the decode attention CTA writes planes with all its threads");
 constexpr int kMaxParts = 16;  // split-K partial tiles a reader sums
 
@@ -283,15 +294,40 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const f
                                                                       uint32_t* __restrict__ head_done, int nt,
                                                                       uint8_t* __restrict__ planes,
                                                                       float* __restrict__ inv) {
-    griddep_launch_dependents();
-    griddep_wait();
     __shared__ __align__(16) float qs[G][kHeadDim];
+    __shared__ __align__(16) float ps[kAttnWarps][32][G];  // a chunk's probabilities, [key][head]
+    __shared__ int32_t pid[kAttnPid];
     __shared__ float ms[kAttnWarps][G], ls[kAttnWarps][G];
-    __shared__ float os[kAttnWarps][G][kHeadDim];
+    extern __shared__ __align__(16) float kvs[];  // [K | V][kAttnWin][kKVPad]; then the warps' outputs
+    static_assert(kAttnWarps * G * kHeadDim <= 2 * kAttnWin * kKVPad, "the warps' outputs fit the window");
+    griddep_launch_dependents();
     const int s = blockIdx.x, g = blockIdx.y;
-    if (pg.seq_cnt[s] == 0) return;  // the whole CTA: the sequence is idle this step
+    const bool idle = pg.seq_cnt[s] == 0;  // the whole CTA: the sequence has no token this step
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = pg.seq_len[s];
+    const int pos = pg.seq_len[s], n = pos + 1;
+    const size_t head = static_cast<size_t>(g) * kHeadDim;
+    const int32_t* table = pg.table + static_cast<size_t>(s) * pg.max_pages;
+    if (!idle)
+        for (int i = threadIdx.x; i < min((n + kPage - 1) / kPage, kAttnPid); i += blockDim.x) pid[i] = table[i];
+    __syncthreads();
+    auto slot = [&](int j) {  // cache offset of position j's row of this kv head
+        const int page = j / kPage < kAttnPid ? pid[j / kPage] : table[j / kPage];
+        return (static_cast<size_t>(page) * kPage + j % kPage) * kvd + head;
+    };
+    // window w's rows, 16 sixteen-byte pieces of K, then of V, per position;
+    // the new position only after it is written (w > 0)
+    auto stage = [&](int w) {
+        const int j0 = w * kAttnWin, cnt = min(n - j0, kAttnWin);
+        for (int e = threadIdx.x; e < cnt * 32; e += blockDim.x) {
+            const int jr = e >> 5, c = e & 31, isv = c >> 4;
+            if (j0 + jr == pos && w == 0) continue;
+            cp_async16(kvs + (isv * kAttnWin + jr) * kKVPad + (c & 15) * 4, (isv ? vc : kc) + slot(j0 + jr) + (c & 15) * 4);
+        }
+        cp_async_commit();
+    };
+    if (!idle) stage(0);
+    griddep_wait();
+    if (idle) return;
     const int64_t r = pg.seq_row0[s];  // the sequence's row in this step
     const float* row = qkv + r * ld;
     auto val = [&](int c) {  // partial loads first, then the sum in partial order
@@ -304,8 +340,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const f
             if (j < parts) acc = __fadd_rn(acc, v[j]);
         return acc;
     };
-    const size_t head = static_cast<size_t>(g) * kHeadDim;
-    const size_t cache_row = kv_slot(pg, s, pos, kvd) + head;
+    const size_t cache_row = slot(pos);
+    float* const win_k = pos < kAttnWin ? kvs + pos * kKVPad : nullptr;  // the new row's staged copy, if in window 0
     for (int pr = threadIdx.x; pr < (group + 1) * (kHeadDim / 2); pr += blockDim.x) {
         const bool isq = pr < group * (kHeadDim / 2);
         const int i = pr % (kHeadDim / 2);  // rotation pair within the head
@@ -321,11 +357,19 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const f
         } else {
             kc[cache_row + 2 * i] = e0;
             kc[cache_row + 2 * i + 1] = e1;
+            if (win_k) {
+                win_k[2 * i] = e0;
+                win_k[2 * i + 1] = e1;
+            }
         }
     }
-    for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) vc[cache_row + d] = val(H + kvd + g * kHeadDim + d);
+    for (int d = threadIdx.x; d < kHeadDim; d += blockDim.x) {
+        const float v = val(H + kvd + g * kHeadDim + d);
+        vc[cache_row + d] = v;
+        if (win_k) win_k[kAttnWin * kKVPad + d] = v;
+    }
     for (int e = group * kHeadDim + threadIdx.x; e < G * kHeadDim; e += blockDim.x) qs[e / kHeadDim][e % kHeadDim] = 0.f;
-    __syncthreads();  // queries staged; the new key and value visible to the CTA
+    __threadfence_block();  // the new row reaches the cache before a later window's copy reads it back
     float m[G], l[G], o0[G], o1[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
@@ -334,70 +378,96 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const f
         o0[h] = 0.f;
         o1[h] = 0.f;
     }
-    const int n = pos + 1;
-    for (int c0 = warp * 32; c0 < n; c0 += kAttnWarps * 32) {
-        const int j = c0 + lane;
-        const bool valid = j < n;
-        float p[G];
+    const float* kb = kvs;
+    const float* vb = kvs + kAttnWin * kKVPad;
+    for (int j0 = 0; j0 < n; j0 += kAttnWin) {
+        if (j0 > 0) {
+            __syncthreads();  // every warp is done with the previous window
+            stage(j0 / kAttnWin);
+        }
+        cp_async_wait_all();
+        __syncthreads();  // the window landed (and, at the first, the queries and the new row are staged)
+        const int cnt = min(n - j0, kAttnWin);
+        for (int c0 = warp * 32; c0 < cnt; c0 += kAttnWarps * 32) {
+            const int jr = c0 + lane;
+            const bool valid = jr < cnt;
+            float p[G];
 #pragma unroll
-        for (int h = 0; h < G; ++h) p[h] = 0.f;
-        const float4* kr = reinterpret_cast<const float4*>(kc + kv_slot(pg, s, valid ? j : c0, kvd) + head);
+            for (int h = 0; h < G; ++h) p[h] = 0.f;
+            const float4* kr = reinterpret_cast<const float4*>(kb + (valid ? jr : c0) * kKVPad);
 #pragma unroll 4
-        for (int i = 0; i < kHeadDim / 4; ++i) {
-            const float4 kv = kr[i];
+            for (int i = 0; i < kHeadDim / 4; ++i) {
+                const float4 kv = kr[i];
+#pragma unroll
+                for (int h = 0; h < G; ++h) {
+                    const float4 qv = reinterpret_cast<const float4*>(qs[h])[i];
+                    p[h] = fmaf(qv.x, kv.x, p[h]);
+                    p[h] = fmaf(qv.y, kv.y, p[h]);
+                    p[h] = fmaf(qv.z, kv.z, p[h]);
+                    p[h] = fmaf(qv.w, kv.w, p[h]);
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < G; ++h) p[h] = valid ? p[h] / 8.0f : -INFINITY;  // sqrt(64)
 #pragma unroll
             for (int h = 0; h < G; ++h) {
-                const float4 qv = reinterpret_cast<const float4*>(qs[h])[i];
-                p[h] = fmaf(qv.x, kv.x, p[h]);
-                p[h] = fmaf(qv.y, kv.y, p[h]);
-                p[h] = fmaf(qv.z, kv.z, p[h]);
-                p[h] = fmaf(qv.w, kv.w, p[h]);
+                float mx = p[h];
+#pragma unroll
+                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float m_new = fmaxf(m[h], mx);  // finite: lane 0 of the chunk is a valid key
+                const float pj = valid ? expf(p[h] - m_new) : 0.f;
+                float sum = pj;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                const float corr = expf(m[h] - m_new);
+                l[h] = l[h] * corr + sum;
+                o0[h] *= corr;
+                o1[h] *= corr;
+                m[h] = m_new;
+                ps[warp][lane][h] = pj;
             }
-        }
+            __syncwarp();
+            // value rows eight keys at a time, folded in key order, with the
+            // keys' probabilities of every head read back as vectors
+            const int nc = min(32, cnt - c0);
+            for (int u0 = 0; u0 < nc; u0 += 8) {
+                float v0[8], v1[8];
 #pragma unroll
-        for (int h = 0; h < G; ++h) p[h] = valid ? p[h] / 8.0f : -INFINITY;  // sqrt(64)
+                for (int u = 0; u < 8; ++u) {
+                    const float* vr = vb + (c0 + min(u0 + u, nc - 1)) * kKVPad;
+                    v0[u] = vr[lane];
+                    v1[u] = vr[lane + 32];
+                }
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-            float mx = p[h];
+                for (int u = 0; u < 8; ++u) {
+                    if (u0 + u < nc) {
+                        float pt[G];
+                        if constexpr (G % 4 == 0) {
 #pragma unroll
-            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            const float m_new = fmaxf(m[h], mx);  // finite: lane 0 of the chunk is a valid key
-            const float pj = valid ? expf(p[h] - m_new) : 0.f;
-            float ps = pj;
+                            for (int h4 = 0; h4 < G / 4; ++h4) {
+                                const float4 q4 = reinterpret_cast<const float4*>(ps[warp][u0 + u])[h4];
+                                pt[4 * h4] = q4.x;
+                                pt[4 * h4 + 1] = q4.y;
+                                pt[4 * h4 + 2] = q4.z;
+                                pt[4 * h4 + 3] = q4.w;
+                            }
+                        } else {
 #pragma unroll
-            for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-            const float corr = expf(m[h] - m_new);
-            l[h] = l[h] * corr + ps;
-            o0[h] *= corr;
-            o1[h] *= corr;
-            m[h] = m_new;
-            p[h] = pj;
-        }
-        // value rows eight keys at a time: the loads of the eight are in
-        // flight together, then folded in key order
-        const int nc = min(32, n - c0);
-        for (int j0 = 0; j0 < nc; j0 += 8) {
-            float v0[8], v1[8];
+                            for (int h = 0; h < G; ++h) pt[h] = ps[warp][u0 + u][h];
+                        }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int jj = min(j0 + u, nc - 1);
-                const float* vr = vc + kv_slot(pg, s, c0 + jj, kvd) + head;
-                v0[u] = vr[lane];
-                v1[u] = vr[lane + 32];
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                if (j0 + u < nc) {
-#pragma unroll
-                    for (int h = 0; h < G; ++h) {
-                        const float pt = __shfl_sync(0xffffffffu, p[h], j0 + u);
-                        o0[h] = fmaf(pt, v0[u], o0[h]);
-                        o1[h] = fmaf(pt, v1[u], o1[h]);
+                        for (int h = 0; h < G; ++h) {
+                            o0[h] = fmaf(pt[h], v0[u], o0[h]);
+                            o1[h] = fmaf(pt[h], v1[u], o1[h]);
+                        }
                     }
                 }
             }
+            __syncwarp();  // ps is rewritten by the warp's next chunk
         }
     }
+    float(*os)[G][kHeadDim] = reinterpret_cast<float(*)[G][kHeadDim]>(kvs);  // [warp][head][dim]
+    __syncthreads();  // every warp is done with the window
 #pragma unroll
     for (int h = 0; h < G; ++h) {
         if (lane == 0) {
@@ -648,8 +718,13 @@ void attn_decode(tir_batch* b, const Pages& pg, int64_t rows, int parts, int gro
     const unsigned th = kAttnWarps * 32;
     const int64_t part = rows * ldq;
 #define TIR_ATTN(GM)                                                                                                   \
-    launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), 0, b->stream, true, b->QKV, parts, part, ldq, pg, H, KVD,    \
-                  group, b->rcos, b->rsin, kc, vc, b->ATT, b->head_done, gemm_token_tile(rows), b->planes, b->inv)
+    do {                                                                                                               \
+        cudaFuncSetAttribute(attn_decode_kernel<GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,                      \
+                             static_cast<int>(kAttnDynSmem));                                                          \
+        launch_kernel(attn_decode_kernel<GM>, grid, dim3(th), kAttnDynSmem, b->stream, true, b->QKV, parts, part, ldq, \
+                      pg, H, KVD, group, b->rcos, b->rsin, kc, vc, b->ATT, b->head_done, gemm_token_tile(rows),        \
+                      b->planes, b->inv);                                                                              \
+    } while (0)
     if (group <= 1)
         TIR_ATTN(1);
     else if (group <= 2)

@@ -17,11 +17,12 @@
 // Q8_0 block (8.5 KB) and the step's pre-split activation planes (NT x 256 B)
 // with TMA bulk copies into a ring of 2 (NT = 256) or 6 (NT = 64) stages
 // (each SM's copy engine spends a fixed time per copy, so the copies are few
-// and large); warps 2-5 expand each raw block into the 128B-swizzled f16
-// hi/lo A planes of a separate 2-stage ring, in packed f16 arithmetic (two
-// instructions per weight); one thread of warp 1 issues the 12 tcgen05.mma of
-// the step (4 K sub-steps x 3 passes) and commits both stages back; after the
-// last step warps 2-5 read the f32 accumulator out of TMEM.
+// and large); the kGConvWarps converter warps expand each raw block into the
+// 128B-swizzled f16 hi/lo A planes of a separate 2-stage ring, in packed f16
+// arithmetic (two instructions per weight); one thread of warp 1 issues the
+// tcgen05.mma of the step (4 K sub-steps x 3 passes) and commits both stages
+// back; after the last step the converter warps read the f32 accumulator out
+// of TMEM.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -41,8 +42,11 @@ namespace tir {
 namespace {
 
 constexpr int kGM = 128;    // weight rows per tile (UMMA M)
-constexpr int kGConvWarps = 8;  // weight converters, then the epilogue (two warps per TMEM lane quarter)
+constexpr int kGConvWarps = 16;  // weight converters, then the epilogue (kGRowThreads warps per TMEM lane quarter)
 constexpr int kGThreads = 64 + 32 * kGConvWarps;
+constexpr int kGRowThreads = kGConvWarps / 4;     // converter threads per weight row
+constexpr int kGConvCols = kGKS / kGRowThreads;    // columns of a row one converter thread expands
+static_assert(kGConvWarps % 4 == 0 && kGConvCols % 8 == 0, "converters cover whole 16-byte chunks");
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
 constexpr int kGPlaneA = kGM * kGKS * 2;            // one f16 weight plane of a stage (16 KB)
 constexpr uint32_t kGErrTimeout = 25;
@@ -253,18 +257,19 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
             umma_commit(&s.acc);
         }
     } else {
-        // ---- converters: threads r and r + 128 expand weight row r of each
-        // step, columns 0..31 and 32..63.  The raw
+        // ---- converters: threads r + 128 j (j < kGRowThreads) expand weight
+        // row r of each step, columns [kGConvCols j, kGConvCols (j + 1)).  The raw
         // block holds q + 128 as bytes and f16 scales already multiplied by
         // the row's 2^kw, so a = q * s' (at most 19 significant bits, below
         // 2^15) splits in packed f16 arithmetic: hi = RN(q * s'), and
         // lo = q * s' - hi, exact in one fused multiply-add (at most 8
         // significant bits, all at or above the last bit of s').  Bytes become
         // f16 by the magic-number route: 0x64 << 8 | b is the f16 1024 + b.
-        const int r = (tid - 64) & (kGM - 1), hc = (tid - 64) >> 7;  // row, column half
-        uint32_t offs[4];
+        constexpr int kCh = kGConvCols / 8;
+        const int r = (tid - 64) & (kGM - 1), hc = (tid - 64) >> 7;  // row, column part
+        uint32_t offs[kCh];
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) offs[ch] = sw128_offset(r, (4 * hc + ch) * 8);
+        for (int ch = 0; ch < kCh; ++ch) offs[ch] = sw128_offset(r, hc * kGConvCols + ch * 8);
         const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
         bool ok = true;
         for (int i = 0; i < nks && ok; ++i) {
@@ -272,13 +277,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
             ok = gwait(p, &s.full_w[st], (i / kRaw) & 1);
             if (ok && i >= kConv) ok = gwait(p, &s.empty_a[sa], ((i / kConv) - 1) & 1);
             if (ok) {
-                const uint8_t* wq = s.w[st] + r * kGKS + 32 * hc;
+                const uint8_t* wq = s.w[st] + r * kGKS + hc * kGConvCols;
                 const __half2 sc2 = reinterpret_cast<const __half2*>(s.w[st] + kGM * kGKS)[r];
-                const __half2 sc = hc ? __high2half2(sc2) : __low2half2(sc2);
+                const __half2 sc = hc * kGConvCols >= 32 ? __high2half2(sc2) : __low2half2(sc2);
                 uint8_t* ahi = s.a[sa];
                 uint8_t* alo = s.a[sa] + kGPlaneA;
 #pragma unroll
-                for (int ch = 0; ch < 4; ++ch) {  // 8 columns per 16-byte chunk
+                for (int ch = 0; ch < kCh; ++ch) {  // 8 columns per 16-byte chunk
                     const uint2 qv = *reinterpret_cast<const uint2*>(wq + ch * 8);
                     uint4 hv, lv;
                     uint32_t* hp = &hv.x;
@@ -305,8 +310,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
             }
         }
         // ---- epilogue: TMEM lane quarter (warp % 4) holds weight rows 32 q .. 32 q + 31,
-        // read by two warps, each half of the tile's tokens; it reads 2^-kx per
-        // token and may add into y: after earlier work
+        // read by kGRowThreads warps, each a share of the tile's tokens; it reads
+        // 2^-kx per token and may add into y: after earlier work
         griddep_wait();
         for (int i = tid - 64; i < NT; i += 32 * kGConvWarps) s.inv_x[i] = p.x_inv[tt * NT + i];
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kGConvWarps) : "memory");  // the epilogue warps
@@ -321,8 +326,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         // `split` of y ([splits][tokens][y_ld]); the reader adds them up
         float* y = p.y + static_cast<size_t>(split) * p.tokens * p.y_ld;
         if (acc_ok) {  // warp-uniform: the TMEM loads are warp-collective
-            const int half = (warp - 2) >> 2;
-            for (int c0 = half * (NT / 2); c0 < (half + 1) * (NT / 2); c0 += 16) {
+            const int part = (warp - 2) >> 2;  // this warp's share of the tile's tokens
+            for (int c0 = part * (NT / kGRowThreads); c0 < (part + 1) * (NT / kGRowThreads); c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + (static_cast<uint32_t>(q * 32) << 16) + c0, v);
                 if constexpr (GemmCfg<NT>::kMergeLo) {  // + a_hi x x_lo from columns NT..2 NT
