@@ -13,13 +13,15 @@
 // product, and the powers of two are divided out exactly in the epilogue.
 //
 // Data flow per CTA (one 128-row weight tile x one NT-token tile, NT = 256,
-// or 64 for small batches; K in steps of 64): warp 0 streams each step's raw
-// Q8_0 block (8.5 KB) and the step's pre-split activation planes (NT x 256 B)
-// with TMA bulk copies into a ring of 2 (NT = 256) or 6 (NT = 64) stages
-// (each SM's copy engine spends a fixed time per copy, so the copies are few
-// and large); the kGConvWarps converter warps expand each raw block into the
-// 128B-swizzled f16 hi/lo A planes of a separate 2-stage ring, in packed f16
-// arithmetic (two instructions per weight); one thread of warp 1 issues the
+// or 64 for small batches; K in steps of 64): warp 0 streams each step's
+// pre-split activation planes (NT x 256 B) with one TMA bulk copy into a ring
+// of 2 (NT = 256) or 6 (NT = 64) stages; each of the kGConvWarps converter
+// warps' threads copies its own 16 bytes of the step's raw Q8_0 block (and
+// the row's scales) with cp.async into a private ring a few steps ahead (each
+// SM's copy engine spends a fixed time per copy, so a step takes one TMA copy,
+// not two) and expands them into the 128B-swizzled f16 hi/lo A planes of a
+// separate 2-stage ring, in packed f16 arithmetic (two instructions per
+// weight); one thread of warp 1 issues the
 // tcgen05.mma of the step (4 K sub-steps x 3 passes) and commits both stages
 // back; after the last step the converter warps read the f32 accumulator out
 // of TMEM.
@@ -46,7 +48,7 @@ constexpr int kGConvWarps = 16;  // weight converters, then the epilogue (kGRowT
 constexpr int kGThreads = 64 + 32 * kGConvWarps;
 constexpr int kGRowThreads = kGConvWarps / 4;     // converter threads per weight row
 constexpr int kGConvCols = kGKS / kGRowThreads;    // columns of a row one converter thread expands
-static_assert(kGConvWarps % 4 == 0 && kGConvCols % 8 == 0, "converters cover whole 16-byte chunks");
+static_assert(kGConvWarps % 4 == 0 && kGConvCols == 16, "a converter thread expands 16 columns (one 16-byte copy)");
 constexpr int kGWBytes = kGM * kGKS + kGM * 2 * 2;  // quants + 2 f16 scales per row
 constexpr int kGPlaneA = kGM * kGKS * 2;            // one f16 weight plane of a stage (16 KB)
 constexpr uint32_t kGErrTimeout = 25;
@@ -61,10 +63,15 @@ struct GemmCfg {
     // passes separately (N is at most 256).
     static constexpr bool kMergeLo = 2 * NT <= 256;
     static constexpr int kTmemCols = kMergeLo ? 2 * NT : NT;
-    // TMA ring (raw weight block + activation planes of a K step): deep for
-    // small token tiles, whose steps are short, so that HBM latency is covered.
-    static constexpr int kRaw = NT >= 256 ? 2 : 6;
-    static constexpr int kConv = 2;                  // expanded weight-plane stages
+    // TMA ring of the steps' activation planes.
+    static constexpr int kRaw = NT >= 256 ? 2 : 3;
+    // Each converter thread's own ring of its raw weight bytes (cp.async),
+    // kWStages steps ahead: the weights take no TMA copy (each SM's copy
+    // engine spends a fixed time per copy, and a step then needs only one).
+    static constexpr int kWStages = NT >= 256 ? 3 : 4;
+    // Expanded weight-plane stages: a stage returns to the converters only
+    // when its MMAs have completed, so short steps need more of them.
+    static constexpr int kConv = NT >= 256 ? 2 : 4;
     static constexpr int kPlaneX = NT * kGKS * 2;  // one f16 activation plane of a stage
 };
 
@@ -72,9 +79,10 @@ template <int NT>
 struct GemmSmem {
     using C = GemmCfg<NT>;
     uint8_t a[C::kConv][2 * kGPlaneA];            // weight planes hi | lo (128B-swizzled, K-major)
-    uint8_t x[C::kRaw][2 * C::kPlaneX];           // activation planes hi | lo, as laid out in global
-    uint8_t w[C::kRaw][kGWBytes];                 // raw block of the step (TMA target)
-    uint64_t full_w[C::kRaw], full_x[C::kRaw], empty_raw[C::kRaw], full_a[C::kConv], empty_a[C::kConv], acc;
+    uint8_t x[C::kRaw][2 * C::kPlaneX];           // activation planes hi | lo, as laid out in global (TMA target)
+    uint4 wq[C::kWStages][kGConvWarps * 32];      // each converter thread's 16 quants of a step
+    uint32_t ws[C::kWStages][kGConvWarps * 32];   // ... and its row's two f16 scales
+    uint64_t full_x[C::kRaw], empty_x[C::kRaw], full_a[C::kConv], empty_a[C::kConv], acc;
     uint32_t tmem_base;
     int32_t ok;
     float inv_x[NT];  // 2^-kx of the tile's tokens
@@ -115,6 +123,10 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t adesc, uint64_t
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
+}
+
+__device__ __forceinline__ void cp_async4_ca(void* dst_smem, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -165,9 +177,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     const int nks = min(nks_all, ks0 + p.ks_per_split) - ks0;
     if (tid == 0) {
         for (int i = 0; i < kRaw; ++i) {
-            mbar_init(&s.full_w[i], 1);
             mbar_init(&s.full_x[i], 1);
-            mbar_init(&s.empty_raw[i], kGConvWarps + 1);  // the converter warps + the MMAs' commit
+            mbar_init(&s.empty_x[i], 1);  // the MMAs' commit
         }
         for (int i = 0; i < kConv; ++i) {
             mbar_init(&s.full_a[i], kGConvWarps);
@@ -189,17 +200,11 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
     if (tid == 0) griddep_launch_dependents();
 
     if (warp == 0) {
-        // ---- producer: raw weight block + activation planes of each K step.
-        // The weights do not depend on earlier work of the stream: the first
-        // stages' weight blocks are fetched before waiting for it.
+        // ---- producer: the activation planes of each K step (after the
+        // earlier work of the stream that writes them)
         if (lane == 0) {
-            const uint8_t* wsrc = p.w + (static_cast<size_t>(rt) * nks_all + ks0) * kGWBytes;
             const uint8_t* xsrc = p.xp + (static_cast<size_t>(tt) * nks_all + ks0) * (2 * kGPlaneX);
             const int pre = min(nks, kRaw);
-            for (int i = 0; i < pre; ++i) {
-                mbar_arrive_expect_tx(&s.full_w[i], kGWBytes);
-                bulk_g2s(s.w[i], wsrc + static_cast<size_t>(i) * kGWBytes, kGWBytes, &s.full_w[i]);
-            }
             griddep_wait();
             for (int i = 0; i < pre; ++i) {
                 mbar_arrive_expect_tx(&s.full_x[i], 2 * kGPlaneX);
@@ -208,21 +213,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
             int issued = pre;
             for (int i = pre; i < nks; ++i) {
                 const int st = i % kRaw;
-                if (!gwait(p, &s.empty_raw[st], ((i / kRaw) - 1) & 1)) {
+                if (!gwait(p, &s.empty_x[st], ((i / kRaw) - 1) & 1)) {
                     s.ok = 0;
                     break;
                 }
-                mbar_arrive_expect_tx(&s.full_w[st], kGWBytes);
-                bulk_g2s(s.w[st], wsrc + static_cast<size_t>(i) * kGWBytes, kGWBytes, &s.full_w[st]);
                 mbar_arrive_expect_tx(&s.full_x[st], 2 * kGPlaneX);
                 bulk_g2s(s.x[st], xsrc + static_cast<size_t>(i) * (2 * kGPlaneX), 2 * kGPlaneX, &s.full_x[st]);
                 issued = i + 1;
             }
             // every copy issued lands before the CTA can leave
-            for (int i = max(0, issued - kRaw); i < issued; ++i) {
-                gwait(p, &s.full_w[i % kRaw], (i / kRaw) & 1);
-                gwait(p, &s.full_x[i % kRaw], (i / kRaw) & 1);
-            }
+            for (int i = max(0, issued - kRaw); i < issued; ++i) gwait(p, &s.full_x[i % kRaw], (i / kRaw) & 1);
         }
     } else if (warp == 1) {
         // ---- MMA issue (one thread)
@@ -252,13 +252,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                 }
                 // the weight planes and the activation planes are free once these MMAs completed
                 umma_commit(&s.empty_a[sa]);
-                umma_commit(&s.empty_raw[st]);
+                umma_commit(&s.empty_x[st]);
             }
             umma_commit(&s.acc);
         }
     } else {
         // ---- converters: threads r + 128 j (j < kGRowThreads) expand weight
-        // row r of each step, columns [kGConvCols j, kGConvCols (j + 1)).  The raw
+        // row r of each step, columns [kGConvCols j, kGConvCols (j + 1)),
+        // copying their own 16 quant bytes and the row's scales into their
+        // ring slot kWStages steps ahead (the weights do not depend on
+        // earlier work of the stream, so the first copies go out at once).  The raw
         // block holds q + 128 as bytes and f16 scales already multiplied by
         // the row's 2^kw, so a = q * s' (at most 19 significant bits, below
         // 2^15) splits in packed f16 arithmetic: hi = RN(q * s'), and
@@ -266,25 +269,41 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
         // significant bits, all at or above the last bit of s').  Bytes become
         // f16 by the magic-number route: 0x64 << 8 | b is the f16 1024 + b.
         constexpr int kCh = kGConvCols / 8;
-        const int r = (tid - 64) & (kGM - 1), hc = (tid - 64) >> 7;  // row, column part
+        constexpr int kWS = GemmCfg<NT>::kWStages;
+        const int ct = tid - 64;
+        const int r = ct & (kGM - 1), hc = ct >> 7;  // row, column part
         uint32_t offs[kCh];
 #pragma unroll
         for (int ch = 0; ch < kCh; ++ch) offs[ch] = sw128_offset(r, hc * kGConvCols + ch * 8);
         const __half2 bias = __float2half2_rn(1152.0f);  // 1024 + 128
+        const uint8_t* wsrc = p.w + (static_cast<size_t>(rt) * nks_all + ks0) * kGWBytes + r * kGKS + hc * kGConvCols;
+        const uint8_t* ssrc = p.w + (static_cast<size_t>(rt) * nks_all + ks0) * kGWBytes + kGM * kGKS + r * 4;
+        auto wissue = [&](int i) {  // one commit group per step (empty past the last)
+            if (i < nks) {
+                cp_async16(&s.wq[i % kWS][ct], wsrc + static_cast<size_t>(i) * kGWBytes);
+                cp_async4_ca(&s.ws[i % kWS][ct], ssrc + static_cast<size_t>(i) * kGWBytes);
+            }
+            cp_async_commit();
+        };
+#pragma unroll
+        for (int i = 0; i < kWS; ++i) wissue(i);
         bool ok = true;
         for (int i = 0; i < nks && ok; ++i) {
-            const int st = i % kRaw, sa = i % kConv;
-            ok = gwait(p, &s.full_w[st], (i / kRaw) & 1);
-            if (ok && i >= kConv) ok = gwait(p, &s.empty_a[sa], ((i / kConv) - 1) & 1);
+            const int sa = i % kConv;
+            cp_async_wait<kWS - 1>();  // this thread's copies of step i landed
+            const uint4 q16 = s.wq[i % kWS][ct];
+            const uint32_t s2 = s.ws[i % kWS][ct];
+            wissue(i + kWS);  // into the slot just read
+            if (i >= kConv) ok = gwait(p, &s.empty_a[sa], ((i / kConv) - 1) & 1);
             if (ok) {
-                const uint8_t* wq = s.w[st] + r * kGKS + hc * kGConvCols;
-                const __half2 sc2 = reinterpret_cast<const __half2*>(s.w[st] + kGM * kGKS)[r];
+                const __half2 sc2 = *reinterpret_cast<const __half2*>(&s2);
                 const __half2 sc = hc * kGConvCols >= 32 ? __high2half2(sc2) : __low2half2(sc2);
+                const uint32_t qw[4] = {q16.x, q16.y, q16.z, q16.w};
                 uint8_t* ahi = s.a[sa];
                 uint8_t* alo = s.a[sa] + kGPlaneA;
 #pragma unroll
                 for (int ch = 0; ch < kCh; ++ch) {  // 8 columns per 16-byte chunk
-                    const uint2 qv = *reinterpret_cast<const uint2*>(wq + ch * 8);
+                    const uint2 qv = make_uint2(qw[2 * ch], qw[2 * ch + 1]);
                     uint4 hv, lv;
                     uint32_t* hp = &hv.x;
                     uint32_t* lp = &lv.x;
@@ -304,11 +323,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_q8_kernel(const __grid_cons
                 fence_proxy_async_smem();  // generic-proxy writes, read by the tensor cores
             }
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&s.full_a[sa]);
-                mbar_arrive(&s.empty_raw[st]);
-            }
+            if (lane == 0) mbar_arrive(&s.full_a[sa]);
         }
+        cp_async_wait_all();  // no copy lands after the CTA leaves
         // ---- epilogue: TMEM lane quarter (warp % 4) holds weight rows 32 q .. 32 q + 31,
         // read by kGRowThreads warps, each a share of the tile's tokens; it reads
         // 2^-kx per token and may add into y: after earlier work
