@@ -149,9 +149,12 @@ unsigned long long timeout_ns() {
     return static_cast<unsigned long long>(ms) * 1000000ull;
 }
 
-// Words 0..2 of an op's error block make a launch's waits give up at once;
-// they are cleared on the launch's stream before every launch.  Word 3 keeps
-// the code of a failure until tir_ops_check collects it.
+// Words 0..2 of an op's error block make a launch's waits give up at once.
+// The tensor-core ops clear them on the launch's stream before every launch;
+// a single matvec of the decode kernel leaves them cleared itself (its last
+// CTA to exit, counted in word 4), so back-to-back matvecs pay no extra
+// stream operation.  Word 3 keeps the code of a failure until tir_ops_check
+// collects it.
 static cudaError_t clear_launch_error(uint32_t* err, void* stream) {
     return cudaMemsetAsync(err, 0, 3 * sizeof(uint32_t), static_cast<cudaStream_t>(stream));
 }
@@ -204,8 +207,7 @@ tir_status q8_matmul_stream(const float* x, const uint8_t* quants, const uint16_
                  "counter reset");
     }
     const int grid = d.n_tiles < sms ? d.n_tiles : sms;
-    CUDA_TRY(clear_launch_error(c->error, stream), "error reset");
-    const int rc = decode_launch(p, grid, stream, false);
+    const int rc = decode_launch(p, grid, stream, false);  // words 0..2 are clear: the previous matvec cleared them
     if (rc != 0) return cuda_fail(static_cast<cudaError_t>(rc), "q8 matvec launch");
     return TIR_OK;
 }

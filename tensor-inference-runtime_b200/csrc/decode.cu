@@ -1210,6 +1210,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     for (uint32_t i = 0; i < static_cast<uint32_t>(kWarpSlots); ++i) stream_next(p, s, sw, i, warp, lane);
     run<QACT>(p, s, sw);
     cp_async_wait_all();
+    if (p.phases == nullptr) {
+        // a single matvec: the last CTA to leave clears the launch's error
+        // words 0..2 and the exit count (word 4); word 3 keeps a failure's
+        // code for the host.  Nothing of this launch reads them any more.
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            if (atomicAdd(p.error + 4, 1u) == gridDim.x - 1) {
+                p.error[0] = 0u;
+                p.error[1] = 0u;
+                p.error[2] = 0u;
+                p.error[4] = 0u;
+            }
+        }
+    }
 }
 
 int decode_smem_bytes() { return static_cast<int>(sizeof(Smem)); }

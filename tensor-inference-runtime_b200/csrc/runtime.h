@@ -125,7 +125,8 @@ struct DecodeParams {
     const float* q;            // [H] (written by EPI_QKV)
     uint32_t* counters;        // [n_phases]
     unsigned long long* argmax_part;  // [grid]
-    uint32_t* error;           // [0] code, [1] phase, [2] step, [3] code again (sticky, read by the host)
+    uint32_t* error;           // [0] code, [1] phase, [2] step, [3] code again (sticky, read by the host);
+                               // single matvec (phases == nullptr): [4] exit count, zero between launches
     unsigned long long timeout_ns;
     int32_t hold_phase;        // tests only: this phase's dependency is never met (-1: none)
     // Phase timeline of step `trace_step` (globaltimer ns), NULL when off:

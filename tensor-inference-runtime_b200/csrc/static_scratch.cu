@@ -30,8 +30,9 @@ static __device__ __align__(256) float g_swiglu_scratch[3 * kSwigluStaticMaxF];
 // [0] phase counter (only ever incremented, any start value works);
 // [4..6] error words: must be zero when a matvec starts, so every call
 // clears them on its stream before its first launch; [7] the code of a
-// failed wait, kept until tir_ops_check collects it.
-static __device__ __align__(256) uint32_t g_swiglu_ctl[8];
+// failed wait, kept until tir_ops_check collects it; [8] the matvec's exit
+// count (zero between launches: the last CTA to leave resets it).
+static __device__ __align__(256) uint32_t g_swiglu_ctl[16];
 
 namespace {
 
