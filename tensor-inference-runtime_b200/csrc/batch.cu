@@ -495,12 +495,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(const f
     __shared__ bool last;
     __syncthreads();  // the CTA's part of the row is written
     if (threadIdx.x == 0) {
-        __threadfence();  // ... and visible before the count
-        last = atomicAdd(&head_done[s], 1u) == gridDim.y - 1;
-        if (last) {
-            head_done[s] = 0;  // ready for the next launch
-            __threadfence();   // the other heads' parts visible to this CTA
-        }
+        // acquire-release count: this CTA's part is visible before it, and the
+        // last CTA sees every other head's part
+        last = atom_add_acq_rel_gpu(&head_done[s], 1u) == gridDim.y - 1;
+        if (last) head_done[s] = 0;  // ready for the next launch
     }
     __syncthreads();
     if (!last) return;

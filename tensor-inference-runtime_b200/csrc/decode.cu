@@ -986,13 +986,14 @@ __device__ __forceinline__ bool attention_phase(const DecodeParams& p, Smem& s, 
     if (S > kReaderCombineMaxSplits) {
         cbar();
         if (tid == 0) {
-            __threadfence();
-            const uint32_t old = atomicAdd(p.attn_cnt + d.layer * p.kv_heads + g, 1u);
+            // acquire-release count: this CTA's records (ordered before it by
+            // the barrier) are visible before it, and the last one sees every
+            // record
+            const uint32_t old = atom_add_acq_rel_gpu(p.attn_cnt + d.layer * p.kv_heads + g, 1u);
             s.attn_last = (old == static_cast<uint32_t>(S - 1)) ? 1 : 0;
         }
         cbar();
         if (s.attn_last) {
-            __threadfence();
             for (int h = warp; h < group; h += kWarps) {
                 const float* base = p.attn_part + (static_cast<size_t>(g) * p.max_splits * group + h) * kAttnRec;
                 const size_t jstride = static_cast<size_t>(group) * kAttnRec;

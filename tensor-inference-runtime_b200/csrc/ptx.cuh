@@ -91,6 +91,16 @@ __device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Acquire-release add (returns the old value): the caller's earlier writes
+// (and those ordered before them by a CTA barrier) are visible before the
+// add, and what the earlier adders released is visible to the caller after
+// it: "last one to arrive" counters need no separate full fence.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Asynchronous 16-byte copy global -> shared (L1 bypassed), tracked by the
 // issuing thread's commit groups.
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
