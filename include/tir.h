@@ -404,9 +404,10 @@ tir_status tir_attention(const float *q, const float *k_cache, const float *v_ca
  * cannot be returned by the call itself.  tir_ops_check synchronises `stream`
  * and returns TIR_ERR_TIMEOUT if any op launched on the current device since
  * the last check recorded one (tir_q8_matmul*, tir_swiglu*,
- * tir_q8_matmul_batch), clearing the record; TIR_OK otherwise.  Each op
- * clears its launch's own error words first, so one failure does not make
- * later calls skip their work.  Runtime extension; no counterpart in the
+ * tir_q8_matmul_batch), clearing the record; TIR_OK otherwise.  No launch
+ * starts with an earlier launch's failure in its error words (a matvec's
+ * last CTA to exit clears them; the tensor-core op clears them before it
+ * starts), so one failure does not make later calls skip their work.  Runtime extension; no counterpart in the
  * reference, whose ops are synchronous CPU code. */
 tir_status tir_ops_check(void *stream);
 
