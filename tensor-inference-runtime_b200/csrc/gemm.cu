@@ -15,12 +15,12 @@
 // Data flow per CTA (one 128-row weight tile x one NT-token tile, NT = 256,
 // or 64 for small batches; K in steps of 64): warp 0 streams each step's
 // pre-split activation planes (NT x 256 B) with one TMA bulk copy into a ring
-// of 2 (NT = 256) or 6 (NT = 64) stages; each of the kGConvWarps converter
-// warps' threads copies its own 16 bytes of the step's raw Q8_0 block (and
-// the row's scales) with cp.async into a private ring a few steps ahead (each
-// SM's copy engine spends a fixed time per copy, so a step takes one TMA copy,
-// not two) and expands them into the 128B-swizzled f16 hi/lo A planes of a
-// separate 2-stage ring, in packed f16 arithmetic (two instructions per
+// of GemmCfg::kRaw stages; each of the kGConvWarps converter warps' threads
+// copies its own 16 bytes of the step's raw Q8_0 block (and the row's scales)
+// with cp.async into a private ring kWStages steps ahead (each SM's copy
+// engine spends a fixed time per copy, so a step takes one TMA copy, not two)
+// and expands them into the 128B-swizzled f16 hi/lo A planes of a separate
+// ring of kConv stages, in packed f16 arithmetic (two instructions per
 // weight); one thread of warp 1 issues the
 // tcgen05.mma of the step (4 K sub-steps x 3 passes) and commits both stages
 // back; after the last step the converter warps read the f32 accumulator out
