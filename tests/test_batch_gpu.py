@@ -19,7 +19,10 @@ def tiny(cuda, tirlib, orc, tiny_path):
     m.close()
 
 
-@pytest.mark.parametrize("n_seqs,n_prompt,cap", [(3, 5, 10), (2, 40, 6), (1, 1, 4)])
+# (2, 380, 12): decode positions 380-391 walk three shared-memory windows of
+# earlier key/value rows in the decode attention (the last one staged after
+# the kernel's dependency wait, with the new row read back from the cache)
+@pytest.mark.parametrize("n_seqs,n_prompt,cap", [(3, 5, 10), (2, 40, 6), (1, 1, 4), (2, 380, 12)])
 def test_batch_generate_matches_oracle_per_sequence(tirlib, orc, tiny, n_seqs, n_prompt, cap):
     m, om = tiny
     vocab = m.info["vocab"]
