@@ -332,7 +332,9 @@ tir_status tir_q8_matmul_tiled(const float *x, const uint8_t *w, float *out, int
  * tensor-core layout: tir_q8_gemm_bytes(n, k) bytes plus tir_q8_gemm_rows(n)
  * floats (a power of two per row), prepared once from Q8_0 blocks on the
  * device.  Then y[t][j] = sum_c x[t][c] * W[j][c] (f32, y row stride n) for
- * t < tokens; k must be a multiple of 64. */
+ * t < tokens; k must be a multiple of 64 and at most 6144 (one activation
+ * row is split into the matmul's f16 planes by one CTA, 24 values per
+ * thread); larger k returns TIR_ERR_UNSUPPORTED_SHAPE. */
 int64_t tir_q8_gemm_bytes(int64_t n, int64_t k);
 int64_t tir_q8_gemm_rows(int64_t n);
 tir_status tir_q8_gemm_prepare(const uint8_t *blocks, int64_t n, int64_t k, uint8_t *w, float *w_pow2,

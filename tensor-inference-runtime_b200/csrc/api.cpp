@@ -1216,8 +1216,9 @@ tir_status tir_q8_gemm_prepare(const uint8_t* blocks, int64_t n, int64_t k, uint
 tir_status tir_q8_matmul_batch(const float* x, int64_t tokens, const uint8_t* w, const float* w_pow2, float* y,
                                int64_t n, int64_t k, void* stream) {
     clear_error();
-    if (tokens < 0 || n <= 0 || k <= 0 || k % 64 != 0 || n > INT32_MAX / 2 || tokens > INT32_MAX / 2)
-        return fail(TIR_ERR_UNSUPPORTED_SHAPE, "batched q8 matmul needs n > 0 and k a positive multiple of 64");
+    if (tokens < 0 || n <= 0 || k <= 0 || k % 64 != 0 || k > kMaxK || n > INT32_MAX / 2 || tokens > INT32_MAX / 2)
+        return fail(TIR_ERR_UNSUPPORTED_SHAPE,
+                    "batched q8 matmul needs n > 0 and k a positive multiple of 64, at most " + std::to_string(kMaxK));
     if (!x || !w || !w_pow2 || !y) return fail(TIR_ERR_INVALID_ARG, "null argument");
     if (tokens == 0) return TIR_OK;
     int dev = 0;

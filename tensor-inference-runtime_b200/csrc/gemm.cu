@@ -41,6 +41,10 @@
 
 namespace tir {
 
+// The plane writers keep a whole activation row in one CTA's registers.
+constexpr int64_t kPlaneMaxK = static_cast<int64_t>(kPlaneMaxChunks) * 8 * kPlaneThreads;
+static_assert(kPlaneMaxK >= kMaxK, "the plane writers cover every row the runtime accepts");
+
 namespace {
 
 constexpr int kGM = 128;    // weight rows per tile (UMMA M)
@@ -570,6 +574,7 @@ int launch_gemm_repack(const uint8_t* blocks, int64_t n, int64_t k, uint8_t* out
 
 int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* planes, float* inv, void* stream,
                          bool pdl) {
+    if (k > kPlaneMaxK) return static_cast<int>(cudaErrorInvalidValue);  // one CTA covers a row
     return static_cast<int>(launch_kernel(gemm_x_planes_kernel, dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))),
                                           dim3(kPlaneThreads), 0, static_cast<cudaStream_t>(stream), pdl, x, tokens, k,
                                           gemm_token_tile(tokens), planes, inv));
@@ -577,6 +582,7 @@ int launch_gemm_x_planes(const float* x, int64_t tokens, int64_t k, uint8_t* pla
 
 int launch_gemm_norm_planes(float* X, float* Y, int y_parts, int64_t y_part, const int32_t* rows, int64_t tokens,
                             int64_t k, const float* w, float eps, uint8_t* planes, float* inv, void* stream, bool pdl) {
+    if (k > kPlaneMaxK) return static_cast<int>(cudaErrorInvalidValue);  // one CTA covers a row
     return static_cast<int>(launch_kernel(gemm_norm_planes_kernel,
                                           dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))), dim3(kPlaneThreads),
                                           0, static_cast<cudaStream_t>(stream), pdl, X, Y, y_parts, y_part, rows, tokens,
@@ -586,6 +592,7 @@ int launch_gemm_norm_planes(float* X, float* Y, int y_parts, int64_t y_part, con
 
 int launch_gemm_silu_planes(float* gu, int parts, int64_t part, int64_t tokens, int64_t f, uint8_t* planes,
                             float* inv, void* stream, bool pdl) {
+    if (f > kPlaneMaxK) return static_cast<int>(cudaErrorInvalidValue);  // one CTA covers a row
     return static_cast<int>(launch_kernel(gemm_silu_planes_kernel,
                                           dim3(static_cast<unsigned>(gemm_tokens_padded(tokens))), dim3(kPlaneThreads),
                                           0, static_cast<cudaStream_t>(stream), pdl, gu, parts, part, tokens, f,

@@ -53,6 +53,10 @@ def test_shape_errors_need_no_device(tirlib):
     with pytest.raises(tirlib.TirError) as e:
         tirlib.attention(0, 0, 0, 0, 8, 2, 32, 4, 16)
     assert e.value.name == "UNSUPPORTED_SHAPE"
+    # the tensor-core matmul's activation planes cover rows of at most 6144
+    with pytest.raises(tirlib.TirError) as e:
+        tirlib.q8_matmul_batch(0, 4, (0, 0), 0, 128, 6144 + 64)
+    assert e.value.name == "UNSUPPORTED_SHAPE"
 
 
 def test_scale_stride(tirlib):
